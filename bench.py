@@ -1,0 +1,330 @@
+"""Decode / prefill throughput of the Qwen3-1.7B-architecture engine on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload W1|W2-4|W2-16|W3] [--impl ours|reference]
+
+A step is one generation of the workload on one GPU: prefill of B prompts of P random token IDs,
+then N new tokens (N-1 decode steps), bf16, random-init weights (N(0, 0.02) matrices, unit norms).
+`value` is decode tokens/s over all ranks (B * (N-1) tokens per step per rank, CUDA-event time of
+the decode phase, max over ranks); prefill tokens/s is reported beside it. Under torchrun each rank
+runs an independent replica on its own GPU (no collective on the data path; weak scaling).
+`e2e` times the public `Engine.generate` call with host (pinned) prompt IDs and host results.
+
+`--impl reference` times the reference algorithm's CPU implementation (the restated reference
+engine in oracle/, bf16, all host threads) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "inference-performance-engineering_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+WORKLOADS = {  # name: (batch, prompt, new tokens, capacity, temperature)
+    "W1": (1, 512, 256, 1024, 0.0),
+    "W2-4": (4, 512, 256, 1024, 0.7),
+    "W2-16": (16, 512, 256, 1024, 0.7),
+    "W3": (1, 4096, 128, 4352, 0.0),
+}
+METRIC = "decode tok/s & % HBM roofline, Qwen3-1.7B bf16 B=1/4/16; prefill tok/s"
+REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+
+def peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": float(data["hbm_gbs"]), "bf16_tflops": float(data["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, index: int):
+        self.index, self.samples, self._stop = index, [], threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        query = "clocks.sm,clocks.max.sm," + ",".join(f"clocks_event_reasons.{r}" for r in REASONS)
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={query}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                fields = [f.strip() for f in out.stdout.strip().split(",")]
+                if len(fields) == 2 + len(REASONS):
+                    self.samples.append(fields)
+            except (OSError, subprocess.SubprocessError):
+                return
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        mhz = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        reasons = sorted({REASONS[i] for s in self.samples for i, v in enumerate(s[2:]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(mhz) if mhz else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def decode_bytes_per_step(config, batch: int, context: float) -> float:
+    """Algorithmic HBM bytes of one decode step: every weight once (bf16) plus the KV cache read
+    at the average context, plus the new K/V rows written."""
+    c = config
+    q, kv = c.num_attention_heads * c.head_dim, c.num_key_value_heads * c.head_dim
+    per_layer = (q + 2 * kv) * c.hidden_size + q * c.hidden_size + 3 * c.intermediate_size * c.hidden_size
+    weights = 2 * (c.num_hidden_layers * per_layer + c.vocab_size * c.hidden_size)
+    kv_token = c.num_hidden_layers * 2 * kv * 2
+    return weights + batch * kv_token * (context + 1)
+
+
+def time_gate_up_kernel(engine, batch: int, repeats: int = 56) -> dict:
+    """Live CUDA-event timing of the dominant decode kernel (fused RMSNorm + gate/up + SiLU*up
+    GEMV) over the engine's real layer weights, cycling layers so every launch streams from HBM."""
+    from ipe_b200 import _native as nat
+
+    c, m = engine.loaded.config, engine._model
+    lib = nat.load()
+    stream = torch.cuda.current_stream()
+    x = torch.randn((batch, c.hidden_size), device="cuda").bfloat16()
+    out = torch.empty((batch, c.intermediate_size), dtype=torch.bfloat16, device="cuda")
+    layers = m.layers
+
+    def launch(i):
+        layer = layers[i % len(layers)]
+        nat.check(lib.ipe_rmsnorm_gate_up_silu(x.data_ptr(), layer.ptr["post_norm"], layer.ptr["w_gate_up"],
+                                               out.data_ptr(), batch, c.hidden_size, c.intermediate_size,
+                                               c.rms_norm_eps, stream.cuda_stream), "gate_up")
+
+    for i in range(len(layers)):
+        launch(i)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record(stream)
+    for i in range(repeats):
+        launch(i)
+    end.record(stream)
+    end.synchronize()
+    seconds = start.elapsed_time(end) / 1e3 / repeats
+    algorithmic = 2 * c.intermediate_size * c.hidden_size * 2 + batch * (c.hidden_size + c.intermediate_size) * 2
+    return {"kernel": "gemv_kernel<SiluMul> (ipe_rmsnorm_gate_up_silu)", "seconds": seconds, "bytes": algorithmic}
+
+
+def run_ours(args, rank: int, world: int) -> dict | None:
+    from ipe_b200 import Engine, QWEN3_1_7B
+    from ipe_b200.synthetic import random_model
+
+    batch, prompt, new, capacity, temperature = WORKLOADS[args.workload]
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(device)
+    loaded = random_model(QWEN3_1_7B, seed=0, device=device, generator_device=device)
+    engine = Engine(loaded, batch=batch, capacity=capacity)
+    ids_host = torch.randint(0, QWEN3_1_7B.vocab_size, (batch, prompt), generator=torch.Generator().manual_seed(0))
+    ids_dev = ids_host.to(device)
+    ids_pinned = ids_host.pin_memory()
+    stream = torch.cuda.current_stream()
+
+    def one_step(times):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        engine._generate_on_device(ids_dev, new, temperature, 1234, after_prefill=lambda: e1.record(stream))
+        e2.record(stream)
+        times.append((e0, e1, e2))
+
+    for _ in range(args.warmup):
+        one_step([])
+    torch.cuda.synchronize()
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+    records = []
+    with ClockSampler(device.index) as clocks:
+        for _ in range(args.steps):
+            one_step(records)
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    prefill_s = sum(a.elapsed_time(b) for a, b, _ in records) / 1e3
+    decode_s = sum(b.elapsed_time(c) for _, b, c in records) / 1e3
+    total_s = sum(a.elapsed_time(c) for a, _, c in records) / 1e3
+
+    # e2e: the public API with host prompt IDs in pinned memory and host results
+    e2e_records = []
+    for _ in range(max(1, min(args.steps, 3))):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        out = engine.generate(ids_pinned, new, temperature=temperature, seed=1234)
+        e.record(stream)
+        e.synchronize()
+        e2e_records.append(s.elapsed_time(e) / 1e3)
+    assert out.tokens.shape == (batch, new)
+    e2e_s = sum(e2e_records)
+
+    kernel = time_gate_up_kernel(engine, batch)
+    if world > 1:
+        t = torch.tensor([prefill_s, decode_s, total_s, e2e_s, kernel["seconds"]], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_s, decode_s, total_s, e2e_s, kernel["seconds"] = t.tolist()
+    if rank != 0:
+        return None
+
+    pk = peaks()
+    steps = args.steps
+    decode_tokens = world * batch * (new - 1) * steps
+    value = decode_tokens / decode_s
+    context = prompt + (new - 1) / 2
+    step_bytes = decode_bytes_per_step(QWEN3_1_7B, batch, context)
+    decode_gbs = step_bytes * (new - 1) * steps / decode_s / 1e9  # per GPU
+    achieved = kernel["bytes"] / kernel["seconds"] / 1e9
+    launches = engine.kernel_launches(prompt, new)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "decode tok/s", "n_gpus": world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(total_s / steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (random-init N(0,0.02) weights, uniform random prompt IDs)",
+        "config": {"workload": f"{args.workload}: Qwen3-1.7B arch bf16, batch {batch}, prompt {prompt}, "
+                               f"{new} new tokens, capacity {capacity}, temperature {temperature}",
+                   "batch_per_gpu": batch, "prompt": prompt, "new_tokens": new, "capacity": capacity,
+                   "parallelism": f"dp{world} (independent replicas)",
+                   "l2": "weights 3.44 GB per step > 126 MB L2 (no flush needed)"},
+        "prefill_tok_s": round(world * batch * prompt * steps / prefill_s, 1),
+        "decode_ms_per_token": round(decode_s / ((new - 1) * steps) * 1e3, 4),
+        "decode_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(decode_gbs, 1), "peak_gbs": pk["hbm_gbs"],
+                       "frac": round(decode_gbs / pk["hbm_gbs"], 4), "peak_source": pk["source"]},
+        "roofline": {"kernel": kernel["kernel"], "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
+                     "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "bytes_per_launch": kernel["bytes"], "seconds_per_launch": kernel["seconds"],
+                     "peak_source": pk["source"]},
+        "e2e": {"value": round(world * batch * new * len(e2e_records) / e2e_s, 2), "unit": "generated tok/s",
+                "definition": "Engine.generate(pinned host prompt) -> host tokens; prefill + decode + copies",
+                "h2d_bytes_per_step": batch * prompt * 8, "d2h_bytes_per_step": batch * new * 12 + batch * 8},
+        "gpu_launches": launches["generate"] * steps,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args.workload, samples=args.cpu_decode_steps)
+    return line
+
+
+def cpu_baseline(workload: str, samples: int) -> dict:
+    """The reference engine's algorithm (oracle/ restatement, bf16, sdpa) on the host cores:
+    one prefill of the workload's prompt, then `samples` decode steps (bounded sample)."""
+    from ipe_b200 import QWEN3_1_7B
+    from ipe_b200.synthetic import random_model
+    from oracle import qwen3 as oq
+
+    batch, prompt, _, capacity, _ = WORKLOADS[workload]
+    torch.set_num_threads(os.cpu_count() or 1)
+    loaded = random_model(QWEN3_1_7B, seed=0)
+    ids = torch.randint(0, QWEN3_1_7B.vocab_size, (batch, prompt), generator=torch.Generator().manual_seed(0))
+    engine = oq.CachedEngine(loaded, batch=batch, capacity=capacity, dtype=torch.bfloat16, backend="sdpa")
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        logits = engine.prefill(ids)
+        t1 = time.perf_counter()
+        tokens = logits.argmax(-1)
+        logits = engine.decode(tokens)  # warm-up step
+        tokens = logits.argmax(-1)
+        t2 = time.perf_counter()
+        for _ in range(samples):
+            tokens = engine.decode(tokens).argmax(-1)
+        t3 = time.perf_counter()
+    return {"value": round(batch * samples / (t3 - t2), 3), "unit": "decode tok/s", "cores": torch.get_num_threads(),
+            "kind": "port", "prefill_tok_s": round(batch * prompt / (t1 - t0), 2),
+            "sample": f"{workload}: one {batch}x{prompt} prefill, then {samples} decode steps after one warm-up step"}
+
+
+def run_reference(args, rank: int) -> dict | None:
+    """The CPU reference arm: the restated reference engine on all host threads."""
+    if rank != 0:
+        return None
+    from ipe_b200 import QWEN3_1_7B
+    from ipe_b200.synthetic import random_model
+    from oracle import qwen3 as oq
+
+    batch, prompt, _, capacity, _ = WORKLOADS[args.workload]
+    torch.set_num_threads(os.cpu_count() or 1)
+    loaded = random_model(QWEN3_1_7B, seed=0)
+    ids = torch.randint(0, QWEN3_1_7B.vocab_size, (batch, prompt), generator=torch.Generator().manual_seed(0))
+    per_step = 2
+    engine = oq.CachedEngine(loaded, batch=batch, capacity=capacity, dtype=torch.bfloat16, backend="sdpa")
+    with torch.no_grad():
+        t0 = time.perf_counter()
+        tokens = engine.prefill(ids).argmax(-1)
+        prefill_s = time.perf_counter() - t0
+        for _ in range(args.warmup):
+            for _ in range(per_step):
+                tokens = engine.decode(tokens).argmax(-1)
+        t1 = time.perf_counter()
+        for _ in range(args.steps):
+            for _ in range(per_step):
+                tokens = engine.decode(tokens).argmax(-1)
+        elapsed = time.perf_counter() - t1
+    value = batch * per_step * args.steps / elapsed
+    return {"metric": METRIC, "value": round(value, 3), "unit": "decode tok/s", "impl": "reference",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", 1)), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(elapsed / args.steps * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"{args.workload} (bounded CPU sample)", "batch_per_gpu": batch, "prompt": prompt},
+            "prefill_tok_s": round(batch * prompt / prefill_s, 2),
+            "cpu_baseline": {"value": round(value, 3), "unit": "decode tok/s", "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": f"one {batch}x{prompt} prefill, then {per_step} decode steps per step"},
+            "e2e": {"value": round(value, 3), "unit": "decode tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=5)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--workload", default="W1", choices=sorted(WORKLOADS))
+    parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--cpu-decode-steps", type=int, default=8)
+    args = parser.parse_args()
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    if args.impl == "reference":
+        line = run_reference(args, rank)
+    else:
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+        try:
+            line = run_ours(args, rank, world)
+        finally:
+            if world > 1:
+                import torch.distributed as dist
+                dist.destroy_process_group()
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,175 @@
+/* ipe_b200: C-ABI of the B200 (sm_100a) kernels for the dense Qwen3 prefill/decode hot path.
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*. No torch types. Every entry point
+ * validates its arguments on the host, launches on the given stream without synchronising, and
+ * returns an ipe_status; ipe_last_error() gives the message of the calling thread's last failure.
+ * Pointers are device pointers unless stated. "bf16" buffers hold IEEE bfloat16, row-major and
+ * contiguous unless a stride argument says otherwise.
+ *
+ * Each entry point names the reference code it replaces (mamadou-wane/inference-performance-
+ * engineering, src/ipe/...). The reference has no native code: its "interface" for each step is a
+ * PyTorch call inside ops.py / forward.py / engine.py, which these functions implement on the GPU.
+ */
+#ifndef IPE_B200_H
+#define IPE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  IPE_OK = 0,
+  IPE_ERR_ARGUMENT = 1,    /* bad pointer, size or shape: nothing was launched */
+  IPE_ERR_UNSUPPORTED = 2, /* a shape the kernels are not built for */
+  IPE_ERR_CUDA = 3,        /* a CUDA runtime / driver call failed */
+} ipe_status;
+
+/* Linear-layer epilogues of ipe_gemm. */
+typedef enum {
+  IPE_EPI_STORE = 0,    /* C[m,n] = bf16(acc)                                        */
+  IPE_EPI_RESIDUAL = 1, /* C[m,n] = bf16(R[m,n] + bf16(acc)); R may alias C         */
+  IPE_EPI_SILU_MUL = 2, /* B rows interleaved in groups of 64 (gate, up); C[m,n/2] =
+                           bf16(bf16(silu(bf16(gate))) * bf16(up))                  */
+  IPE_EPI_LOGITS = 3,   /* C (fp32)[m,n] = float(bf16(acc))                          */
+} ipe_epilogue;
+
+/* Device-resident step state: int64_t[IPE_STATE_WORDS]. Kernels given a non-null state read the
+ * cache position and the sampling parameters from it instead of their host arguments, so a
+ * captured decode step replays without host work. */
+enum {
+  IPE_STATE_POS = 0,         /* committed positions = position of the token being decoded   */
+  IPE_STATE_STEP = 1,        /* index of the next sampled token in the history buffers      */
+  IPE_STATE_SEED = 2,        /* Gumbel-max sampling seed                                     */
+  IPE_STATE_TEMPERATURE = 3, /* float32 bits in the low word; 0 = greedy                    */
+  IPE_STATE_WORDS = 8,
+};
+
+/* Rows of 64 gate rows followed by 64 up rows, the packing IPE_EPI_SILU_MUL and
+ * ipe_rmsnorm_gate_up_silu expect. */
+#define IPE_GATE_UP_GROUP 64
+/* Floats per sampling partial record written by ipe_lm_head. */
+#define IPE_PARTIAL_WORDS 8
+
+/* ------------------------------------------------------------------ library */
+
+const char* ipe_last_error(void);
+int ipe_abi_version(void);
+/* Reads (and with reset != 0 clears) the device error word of the current device: 0 = none,
+ * 1 = token ID out of range, 2 = cache position out of range, 3 = a bounded wait timed out.
+ * Synchronises the device. */
+int ipe_device_error(int reset, int* out_code);
+
+/* ------------------------------------------------------------------ elementwise */
+
+/* RMSNorm over the last axis, fp32 statistics, two roundings at bf16.
+ * Replaces ipe.ops.rms_norm (src/ipe/ops.py:23-33). dtype: 0 = bf16, 1 = fp32 (x, weight, out). */
+int ipe_rmsnorm(const void* x, const void* weight, void* out, int64_t rows, int width, float eps,
+                int dtype, void* stream);
+
+/* out[i, :] = table[ids[i], :] (bf16). An ID outside [0, vocab) writes zeros and sets device
+ * error 1. Replaces F.embedding in src/ipe/forward.py:125 and src/ipe/engine.py:106. */
+int ipe_embed(const int64_t* ids, int64_t count, const void* table, int64_t vocab, int hidden,
+              void* out, void* stream);
+
+/* Per-head q_norm / k_norm (RMSNorm over head_dim 128), split-half RoPE from bf16 tables, and the
+ * K/V cache append, for `batch` rows of `tokens` tokens at positions start..start+tokens-1 (from
+ * state[IPE_STATE_POS] when state is non-null).
+ *   qkv      bf16 [batch*tokens, (q_heads + 2*kv_heads) * 128]   (q | k | v per token)
+ *   cos/sin  bf16 [>= start+tokens, 128] indexed by absolute position
+ *   q_out    bf16 [batch, q_heads, tokens, 128]
+ *   k/v      bf16 [batch, kv_heads, capacity, 128] (one layer of the cache)
+ * Replaces src/ipe/forward.py:101-109 (qk_norm, apply_rotary, cache write; ops.py:36-63). */
+int ipe_qk_norm_rope_append(const void* qkv, int batch, int tokens, int q_heads, int kv_heads,
+                            const void* q_norm_weight, const void* k_norm_weight,
+                            const void* cos_table, const void* sin_table, int start,
+                            const int64_t* state, void* q_out, void* k_cache, void* v_cache,
+                            int capacity, float eps, void* stream);
+
+/* ------------------------------------------------------------------ decode linear layers
+ * Weight-streaming kernels for batch 1..16 rows (one token each). Weights bf16 [out, in]. */
+
+/* qkv[b,:] = rms_norm(x[b,:]) @ w_qkv^T; w_qkv rows are q_proj | k_proj | v_proj.
+ * Replaces src/ipe/forward.py:100-103 (rms_norm + three F.linear). */
+int ipe_rmsnorm_qkv(const void* x, const void* norm_weight, const void* w_qkv, void* qkv_out,
+                    int batch, int hidden, int qkv_rows, float eps, void* stream);
+
+/* x[b,n] = bf16(x[b,n] + bf16(a[b,:] . w[n,:])). Replaces the o_proj and down_proj residual
+ * updates, src/ipe/forward.py:113 and :115. */
+int ipe_linear_residual(const void* a, const void* w, void* x, int batch, int in_features,
+                        int out_features, void* stream);
+
+/* act[b,j] = bf16(bf16(silu(bf16(g))) * bf16(u)), g / u = rms_norm(x[b]) . gate/up row j;
+ * w_gate_up packed in IPE_GATE_UP_GROUP row groups. Replaces src/ipe/forward.py:114-115
+ * (rms_norm, then ops.swiglu's gate/up/silu/mul, src/ipe/ops.py:104-106). */
+int ipe_rmsnorm_gate_up_silu(const void* x, const void* norm_weight, const void* w_gate_up,
+                             void* act_out, int batch, int hidden, int intermediate, float eps,
+                             void* stream);
+
+/* Final RMSNorm of x rows (row b at x + b*x_row_stride elements), tied LM head, fp32 logits
+ * (bf16-rounded then widened, as the reference), and per-block sampling partials
+ * [ipe_lm_head_parts(vocab)][batch][IPE_PARTIAL_WORDS] for ipe_sample. temperature > 0 adds
+ * Gumbel noise from (seed, position) to the sampling partials only.
+ * Replaces src/ipe/engine.py:110-111 and the first pass of src/ipe/engine.py:28-41. */
+int ipe_lm_head(const void* x, int64_t x_row_stride, const void* norm_weight, const void* embed,
+                float* logits, float* partials, int batch, int hidden, int vocab, float eps,
+                float temperature, uint64_t seed, const int64_t* state, void* stream);
+int ipe_lm_head_parts(int vocab);
+
+/* Token and untempered log-probability per row from the partials: argmax (lowest ID on ties)
+ * when temperature == 0, else Gumbel-max. Writes tokens[b*stride + step] and logprobs[...] with
+ * step = state[IPE_STATE_STEP] (0 without state; the state's step then advances by 1), and
+ * next_tokens[b] (nullable) for the next decode step. Replaces src/ipe/engine.py:28-41. */
+int ipe_sample(const float* partials, const float* logits, int batch, int vocab, float temperature,
+               int64_t* state, int64_t* tokens, float* logprobs, int64_t stride,
+               int64_t* next_tokens, void* stream);
+
+/* The same rule over a logits matrix [rows, vocab] (fp32) already in memory, any number of rows:
+ * tokens[r], logprobs[r]. Gumbel noise is drawn from (seed, row, vocab id). Replaces
+ * ipe.engine.sample (src/ipe/engine.py:28-41) for logits the caller holds. */
+int ipe_sample_logits(const float* logits, int64_t rows, int vocab, float temperature, uint64_t seed,
+                      int64_t* tokens, float* logprobs, void* stream);
+
+/* ------------------------------------------------------------------ attention */
+
+/* Split-KV flash-decode: one query token per row against keys 0..length-1 of the cache
+ * (length = state[IPE_STATE_POS] + 1 when state is non-null), GQA (query head j reads KV head
+ * j / (q_heads / kv_heads)), scale 128^-0.5, fp32 softmax.
+ *   q bf16 [batch, q_heads, 128] -> out bf16 [batch, q_heads * 128]
+ * workspace: ipe_decode_attention_workspace(batch, q_heads, capacity) bytes of device memory.
+ * Replaces ops.attention for decode steps (src/ipe/ops.py:78-101, causal=False). */
+int ipe_decode_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                         int batch, int q_heads, int kv_heads, int capacity, int length,
+                         const int64_t* state, void* workspace, size_t workspace_bytes,
+                         void* stream);
+size_t ipe_decode_attention_workspace(int batch, int q_heads, int capacity);
+
+/* Causal flash-attention over a prompt of `tokens` positions written at cache positions
+ * 0..tokens-1.
+ *   q bf16 [batch, q_heads, tokens, 128] -> out bf16 [batch, tokens, q_heads * 128]
+ * Replaces ops.attention for a prompt (src/ipe/ops.py:78-101, causal=True). */
+int ipe_prefill_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
+                          int batch, int q_heads, int kv_heads, int tokens, int capacity,
+                          void* stream);
+
+/* ------------------------------------------------------------------ tensor-core GEMM */
+
+/* C = epilogue(A @ B^T): A bf16 [m, k], B bf16 [n, k] (both k-contiguous), tcgen05 MMA with
+ * TMEM accumulators fed by TMA. n % 128 == 0, k % 64 == 0, pointers 16-byte aligned.
+ * Replaces the prefill F.linear calls of src/ipe/forward.py:100-115 and the uncached LM head of
+ * src/ipe/forward.py:145-152. */
+int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epilogue,
+             const void* residual, void* stream);
+
+/* ------------------------------------------------------------------ step state */
+
+int ipe_state_set(int64_t* state, int index, int64_t value, void* stream);
+int ipe_state_add(int64_t* state, int index, int64_t delta, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IPE_B200_H */

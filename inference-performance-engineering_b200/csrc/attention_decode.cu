@@ -1,0 +1,188 @@
+// Split-KV flash-decode for grouped-query attention over the preallocated cache.
+//
+// Pass 1: one CTA per (chunk of kChunk keys, KV head, batch row) scores the chunk against every
+// query head that shares the KV head (the K and V rows are read once for the group), and writes
+// the chunk's unnormalised output with its running max and sum. Pass 2 merges the chunks per
+// (batch row, query head). The key count comes from the device step state when one is given, so
+// the grid is sized by capacity and chunks past the current length exit at once.
+#include "common.cuh"
+#include "launch.h"
+
+namespace ipe {
+namespace {
+
+constexpr int kChunk = 32;   // keys per CTA
+constexpr int kThreads = 128;
+constexpr int kMaxGroup = 8;  // query heads per KV head
+constexpr int kRecord = 128 + 2;  // floats per (batch, head, chunk) partial: o[128], max, sum
+constexpr float kScale = 0.08838834764831845f;  // 128 ** -0.5
+
+template <int G>
+__global__ void __launch_bounds__(kThreads) decode_chunk_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
+                                                                const bf16* __restrict__ vc, float* __restrict__ ws,
+                                                                int q_heads, int kv_heads, int capacity, int length_arg,
+                                                                const int64_t* __restrict__ state, int chunks_max) {
+  const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int length = state ? static_cast<int>(state[IPE_STATE_POS]) + 1 : length_arg;
+  const int key0 = chunk * kChunk;
+  if (key0 >= length) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  __shared__ float qs[G][128];
+  __shared__ float sc[G][kChunk];
+  __shared__ float red[8][G][128];
+  __shared__ float stat[G][2];
+
+  for (int i = threadIdx.x; i < G * 128; i += kThreads) {
+    const int g = i / 128, d = i % 128;
+    qs[g][d] = __bfloat162float(q[(static_cast<int64_t>(b) * q_heads + kvh * G + g) * 128 + d]);
+  }
+  __syncthreads();
+
+  const int64_t head_base = (static_cast<int64_t>(b) * kv_heads + kvh) * capacity;
+  // Scores: warp w handles keys key0 + 8w .. +7; 4 lanes per key, 32 dims per lane.
+  {
+    const int kk = warp * 8 + (lane >> 2);
+    const int part = lane & 3;
+    const int key = key0 + kk;
+    float dot[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) dot[g] = 0.f;
+    if (key < length) {
+      const bf16* kr = kc + (head_base + key) * 128 + part * 32;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        float f[8];
+        unpack8(ldg16(kr + v * 8), f);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) dot[g] += f[i] * qs[g][part * 32 + v * 8 + i];
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], 1);
+      dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], 2);
+    }
+    if (part == 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) sc[g][kk] = key < length ? dot[g] * kScale : -INFINITY;
+    }
+  }
+  __syncthreads();
+  // Softmax statistics per query head: warp w handles heads w, w + 4; lane = key.
+  for (int g = warp; g < G; g += kThreads / 32) {
+    const float s = sc[g][lane];
+    const float m = warp_max(s);
+    const float p = s == -INFINITY ? 0.f : expf(s - m);
+    const float l = warp_sum(p);
+    sc[g][lane] = p;
+    if (lane == 0) {
+      stat[g][0] = m;
+      stat[g][1] = l;
+    }
+  }
+  __syncthreads();
+  // P V: thread (key group kg = tid / 16, dim chunk dc = tid % 16) over keys kg, kg+8, kg+16, kg+24.
+  {
+    const int kg = threadIdx.x >> 4, dc = threadIdx.x & 15;
+    float o[G][8];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
+#pragma unroll
+    for (int j = 0; j < kChunk / 8; ++j) {
+      const int kk = kg + 8 * j;
+      const int key = key0 + kk;
+      if (key < length) {
+        float f[8];
+        unpack8(ldg16(vc + (head_base + key) * 128 + dc * 8), f);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float p = sc[g][kk];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[g][i] += p * f[i];
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) red[kg][g][dc * 8 + i] = o[g][i];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * 128; i += kThreads) {
+    const int g = i / 128, d = i % 128;
+    float s = 0.f;
+#pragma unroll
+    for (int kg = 0; kg < 8; ++kg) s += red[kg][g][d];
+    float* rec = ws + ((static_cast<int64_t>(b) * q_heads + kvh * G + g) * chunks_max + chunk) * kRecord;
+    rec[d] = s;
+    if (d == 0) {
+      rec[128] = stat[g][0];
+      rec[129] = stat[g][1];
+    }
+  }
+}
+
+__global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ ws, bf16* __restrict__ out,
+                                                             int q_heads, int length_arg,
+                                                             const int64_t* __restrict__ state, int chunks_max) {
+  const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const int length = state ? static_cast<int>(state[IPE_STATE_POS]) + 1 : length_arg;
+  const int chunks = (length + kChunk - 1) / kChunk;
+  const float* base = ws + (static_cast<int64_t>(b) * q_heads + head) * chunks_max * kRecord;
+  float m = -INFINITY;
+  for (int c = 0; c < chunks; ++c) m = fmaxf(m, base[c * kRecord + 128]);
+  float l = 0.f, o = 0.f;
+  for (int c = 0; c < chunks; ++c) {
+    const float* rec = base + c * kRecord;
+    const float e = expf(rec[128] - m);
+    l += rec[129] * e;
+    o += rec[d] * e;
+  }
+  out[(static_cast<int64_t>(b) * q_heads + head) * 128 + d] = __float2bfloat16_rn(o / l);
+}
+
+template <int G>
+void launch_chunks(dim3 grid, const bf16* q, const bf16* k, const bf16* v, float* ws, int q_heads, int kv_heads,
+                   int capacity, int length, const int64_t* state, int chunks_max, cudaStream_t stream) {
+  decode_chunk_kernel<G><<<grid, kThreads, 0, stream>>>(q, k, v, ws, q_heads, kv_heads, capacity, length, state,
+                                                        chunks_max);
+}
+
+}  // namespace
+
+int decode_attention_chunk() { return kChunk; }
+
+cudaError_t launch_decode_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
+                                    int kv_heads, int capacity, int length, const int64_t* state, float* ws,
+                                    cudaStream_t stream) {
+  const int chunks_max = (capacity + kChunk - 1) / kChunk;
+  const int group = q_heads / kv_heads;
+  const dim3 grid(chunks_max, kv_heads, batch);
+  auto qq = static_cast<const bf16*>(q);
+  auto kk = static_cast<const bf16*>(k);
+  auto vv = static_cast<const bf16*>(v);
+  switch (group) {
+    case 1: launch_chunks<1>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
+    case 2: launch_chunks<2>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
+    case 4: launch_chunks<4>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
+    case 8: launch_chunks<8>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
+    default: return cudaErrorInvalidValue;
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  decode_combine_kernel<<<dim3(q_heads, batch), 128, 0, stream>>>(ws, static_cast<bf16*>(out), q_heads, length, state,
+                                                                   chunks_max);
+  return cudaGetLastError();
+}
+
+size_t decode_attention_workspace_bytes(int batch, int q_heads, int capacity) {
+  const int chunks_max = (capacity + kChunk - 1) / kChunk;
+  return static_cast<size_t>(batch) * q_heads * chunks_max * kRecord * sizeof(float);
+}
+
+}  // namespace ipe

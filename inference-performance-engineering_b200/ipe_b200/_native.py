@@ -1,0 +1,92 @@
+"""ctypes binding of libipe_b200.so, the C-ABI declared in include/ipe_b200.h.
+
+The library is loaded from `ipe_b200/lib/` (built in-tree by `ipe_b200.build`). There is no
+fallback: if the library is missing or fails to load, every call raises `NativeUnavailable`.
+A nonzero ipe_status becomes a RuntimeError carrying `ipe_last_error()`; the entry points check
+their arguments on the host before launching anything.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int, c_int64, c_size_t, c_uint64, c_void_p
+from pathlib import Path
+
+LIBRARY = Path(__file__).resolve().parent / "lib" / "libipe_b200.so"
+
+# enum values of include/ipe_b200.h
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_LOGITS = 0, 1, 2, 3
+STATE_POS, STATE_STEP, STATE_SEED, STATE_TEMPERATURE, STATE_WORDS = 0, 1, 2, 3, 8
+GATE_UP_GROUP = 64
+PARTIAL_WORDS = 8
+
+_P = c_void_p
+SIGNATURES: dict[str, tuple[object, list[object]]] = {
+    "ipe_last_error": (ctypes.c_char_p, []),
+    "ipe_abi_version": (c_int, []),
+    "ipe_device_error": (c_int, [c_int, ctypes.POINTER(c_int)]),
+    "ipe_rmsnorm": (c_int, [_P, _P, _P, c_int64, c_int, c_float, c_int, _P]),
+    "ipe_embed": (c_int, [_P, c_int64, _P, c_int64, c_int, _P, _P]),
+    "ipe_qk_norm_rope_append": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P, _P, _P, _P,
+                                        c_int, c_float, _P]),
+    "ipe_rmsnorm_qkv": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P]),
+    "ipe_linear_residual": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
+    "ipe_rmsnorm_gate_up_silu": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P]),
+    "ipe_lm_head": (c_int, [_P, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_float, c_float, c_uint64, _P, _P]),
+    "ipe_lm_head_parts": (c_int, [c_int]),
+    "ipe_sample": (c_int, [_P, _P, c_int, c_int, c_float, _P, _P, _P, c_int64, _P, _P]),
+    "ipe_sample_logits": (c_int, [_P, c_int64, c_int, c_float, c_uint64, _P, _P, _P]),
+    "ipe_decode_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P, c_size_t, _P]),
+    "ipe_decode_attention_workspace": (c_size_t, [c_int, c_int, c_int]),
+    "ipe_prefill_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
+    "ipe_gemm": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P]),
+    "ipe_state_set": (c_int, [_P, c_int, c_int64, _P]),
+    "ipe_state_add": (c_int, [_P, c_int, c_int64, _P]),
+}
+
+
+class NativeUnavailable(RuntimeError):
+    """The CUDA library could not be loaded; the package has no other implementation."""
+
+
+_lib: ctypes.CDLL | None = None
+_load_error: str | None = None
+
+
+def load() -> ctypes.CDLL:
+    global _lib, _load_error
+    if _lib is not None:
+        return _lib
+    if _load_error is not None:
+        raise NativeUnavailable(_load_error)
+    if not LIBRARY.exists():
+        _load_error = f"{LIBRARY} is missing: build it with `python -m ipe_b200.build` (needs nvcc)"
+        raise NativeUnavailable(_load_error)
+    try:
+        lib = ctypes.CDLL(str(LIBRARY))
+    except OSError as error:
+        _load_error = f"cannot load {LIBRARY}: {error}"
+        raise NativeUnavailable(_load_error) from error
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+def check(status: int, name: str) -> None:
+    if status != 0:
+        message = load().ipe_last_error().decode(errors="replace")
+        raise RuntimeError(f"{name} failed (status {status}): {message}")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(load(), name)(*args), name)
+
+
+def device_error(reset: bool = True) -> int:
+    """The first device-side error code since the last reset (synchronises the device)."""
+    code = c_int(0)
+    call("ipe_device_error", 1 if reset else 0, ctypes.byref(code))
+    return code.value

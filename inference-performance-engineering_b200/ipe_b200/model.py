@@ -1,0 +1,207 @@
+"""Device-side layout of a loaded Qwen3 model, and the per-layer launch sequences.
+
+`PackedModel` turns the reference-layout weights ([out, in] per projection, src/ipe/weights.py)
+into the layout the kernels stream, once per loaded model:
+
+- w_qkv [Q + 2*KV, H]: q_proj | k_proj | v_proj rows, so one pass computes all three;
+- w_gate_up [2*I, H]: gate and up rows interleaved in groups of 64 (IPE_GATE_UP_GROUP), so one
+  CTA (decode) or one 128-column tile (prefill) holds matching gate and up rows for SiLU * up;
+- o_proj, down_proj, the norms and the tied embedding are used in place.
+
+It also builds the bf16 rotary tables the way the reference engine does on the host
+(src/ipe/engine.py:63-67 per position for decode rows; src/ipe/engine.py:78 one call over the
+prompt for prefill).
+
+`prefill_layer` / `decode_layer` issue one decoder layer (src/ipe/forward.py:86-115) as a chain of
+C-ABI launches on the current stream; nothing here computes on the CPU.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ipe_b200 import _native as nat
+from ipe_b200.config import check_supported
+
+
+def rotary_rows(positions: torch.Tensor, head_dim: int, theta: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 cos/sin [T, D] for int64 positions: fp32 angles from inv_freq = 1/theta^(2j/D), split
+    halves (the formula of src/ipe/ops.py:41-53, evaluated on the host as the reference does)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim))
+    angle = positions.to(torch.float32)[:, None] * inv[None, :]
+    angle = torch.cat((angle, angle), dim=-1)
+    return angle.cos().to(torch.bfloat16), angle.sin().to(torch.bfloat16)
+
+
+class PackedLayer:
+    __slots__ = ("in_norm", "post_norm", "q_norm", "k_norm", "w_qkv", "w_o", "w_gate_up", "w_down", "ptr")
+
+    def __init__(self, layer, config):
+        self.in_norm = layer.input_layernorm.contiguous()
+        self.post_norm = layer.post_attention_layernorm.contiguous()
+        self.q_norm = layer.q_norm.contiguous()
+        self.k_norm = layer.k_norm.contiguous()
+        self.w_qkv = torch.cat((layer.q_proj, layer.k_proj, layer.v_proj), dim=0).contiguous()
+        self.w_o = layer.o_proj.contiguous()
+        i, h, g = config.intermediate_size, config.hidden_size, nat.GATE_UP_GROUP
+        gate = layer.gate_proj.reshape(i // g, g, h)
+        up = layer.up_proj.reshape(i // g, g, h)
+        self.w_gate_up = torch.stack((gate, up), dim=1).reshape(2 * i, h).contiguous()
+        self.w_down = layer.down_proj.contiguous()
+        self.ptr = {name: getattr(self, name).data_ptr() for name in
+                    ("in_norm", "post_norm", "q_norm", "k_norm", "w_qkv", "w_o", "w_gate_up", "w_down")}
+
+
+class PackedModel:
+    def __init__(self, loaded):
+        c, w = loaded.config, loaded.weights
+        check_supported(c)
+        self.loaded = loaded
+        self.config = c
+        self.device = w.embed_tokens.device
+        self.embed = w.embed_tokens.contiguous()
+        self.lm_head = w.lm_head.contiguous()
+        self.final_norm = w.norm.contiguous()
+        with torch.no_grad():
+            self.layers = [PackedLayer(layer, c) for layer in w.layers]
+        self.q_rows = c.num_attention_heads * c.head_dim
+        self.kv_rows = c.num_key_value_heads * c.head_dim
+        self.qkv_rows = self.q_rows + 2 * self.kv_rows
+        self._decode_cos: torch.Tensor | None = None
+        self._decode_sin: torch.Tensor | None = None
+        self._prefill_tables: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def decode_rotary(self, capacity: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Per-position rows [capacity, D], each from its own one-position call."""
+        have = 0 if self._decode_cos is None else self._decode_cos.shape[0]
+        if have < capacity:
+            c = self.config
+            rows = [rotary_rows(torch.tensor([p]), c.head_dim, c.rope_theta) for p in range(have, capacity)]
+            cos = torch.cat([r[0] for r in rows]).to(self.device)
+            sin = torch.cat([r[1] for r in rows]).to(self.device)
+            if self._decode_cos is not None:
+                cos, sin = torch.cat((self._decode_cos, cos)), torch.cat((self._decode_sin, sin))
+            self._decode_cos, self._decode_sin = cos.contiguous(), sin.contiguous()
+        return self._decode_cos[:capacity], self._decode_sin[:capacity]
+
+    def prefill_rotary(self, length: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """One call over positions 0..length-1, as the reference's prefill and uncached forward."""
+        if length not in self._prefill_tables:
+            if len(self._prefill_tables) > 8:
+                self._prefill_tables.clear()
+            c = self.config
+            cos, sin = rotary_rows(torch.arange(length), c.head_dim, c.rope_theta)
+            self._prefill_tables[length] = (cos.to(self.device).contiguous(), sin.to(self.device).contiguous())
+        return self._prefill_tables[length]
+
+
+_CACHE: list[tuple[object, PackedModel]] = []
+
+
+def packed_model(loaded) -> PackedModel:
+    """The packed layout of `loaded`, reused while the same LoadedCheckpoint object is in use."""
+    for key, model in _CACHE:
+        if key is loaded:
+            return model
+    model = PackedModel(loaded)
+    _CACHE.clear()
+    _CACHE.append((loaded, model))
+    return model
+
+
+def release_packed_models() -> None:
+    _CACHE.clear()
+
+
+class PrefillBuffers:
+    """Activation buffers for a prompt of batch x length tokens (allocated per prompt size)."""
+
+    def __init__(self, model: PackedModel, tokens: int, batch: int, length: int):
+        c, dev, bf = model.config, model.device, torch.bfloat16
+        self.tokens = tokens
+        self.x = torch.empty((tokens, c.hidden_size), dtype=bf, device=dev)
+        self.h = torch.empty((tokens, c.hidden_size), dtype=bf, device=dev)
+        self.qkv = torch.empty((tokens, model.qkv_rows), dtype=bf, device=dev)
+        self.q = torch.empty((batch, c.num_attention_heads, length, c.head_dim), dtype=bf, device=dev)
+        self.attn = torch.empty((tokens, model.q_rows), dtype=bf, device=dev)
+        self.act = torch.empty((tokens, c.intermediate_size), dtype=bf, device=dev)
+
+
+def prefill_layer(model: PackedModel, index: int, buf: PrefillBuffers, k_layer: torch.Tensor, v_layer: torch.Tensor,
+                  batch: int, length: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor, stream: int) -> None:
+    """One decoder layer over a prompt at positions 0..length-1 (src/ipe/forward.py:86-115, start 0)."""
+    lib = nat.load()
+    c, p = model.config, model.layers[index].ptr
+    m = batch * length
+    h, x = buf.h.data_ptr(), buf.x.data_ptr()
+    eps = c.rms_norm_eps
+    nat.check(lib.ipe_rmsnorm(x, p["in_norm"], h, m, c.hidden_size, eps, 0, stream), "ipe_rmsnorm")
+    nat.check(lib.ipe_gemm(h, p["w_qkv"], buf.qkv.data_ptr(), m, model.qkv_rows, c.hidden_size, nat.EPI_STORE, 0,
+                           stream), "ipe_gemm qkv")
+    nat.check(lib.ipe_qk_norm_rope_append(buf.qkv.data_ptr(), batch, length, c.num_attention_heads,
+                                          c.num_key_value_heads, p["q_norm"], p["k_norm"], cos.data_ptr(),
+                                          sin.data_ptr(), 0, None, buf.q.data_ptr(), k_layer.data_ptr(),
+                                          v_layer.data_ptr(), capacity, eps, stream), "ipe_qk_norm_rope_append")
+    nat.check(lib.ipe_prefill_attention(buf.q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), buf.attn.data_ptr(),
+                                        batch, c.num_attention_heads, c.num_key_value_heads, length, capacity, stream),
+              "ipe_prefill_attention")
+    nat.check(lib.ipe_gemm(buf.attn.data_ptr(), p["w_o"], x, m, c.hidden_size, model.q_rows, nat.EPI_RESIDUAL, x,
+                           stream), "ipe_gemm o_proj")
+    nat.check(lib.ipe_rmsnorm(x, p["post_norm"], h, m, c.hidden_size, eps, 0, stream), "ipe_rmsnorm")
+    nat.check(lib.ipe_gemm(h, p["w_gate_up"], buf.act.data_ptr(), m, 2 * c.intermediate_size, c.hidden_size,
+                           nat.EPI_SILU_MUL, 0, stream), "ipe_gemm gate_up")
+    nat.check(lib.ipe_gemm(buf.act.data_ptr(), p["w_down"], x, m, c.hidden_size, c.intermediate_size,
+                           nat.EPI_RESIDUAL, x, stream), "ipe_gemm down_proj")
+
+
+def run_prefill_layers(model: PackedModel, buf: PrefillBuffers, k: torch.Tensor, v: torch.Tensor, batch: int,
+                       length: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor) -> None:
+    stream = torch.cuda.current_stream().cuda_stream
+    for index in range(len(model.layers)):
+        prefill_layer(model, index, buf, k[index], v[index], batch, length, capacity, cos, sin, stream)
+
+
+class DecodeBuffers:
+    """Fixed buffers of one decode step for up to `batch` rows; allocated once per engine."""
+
+    def __init__(self, model: PackedModel, batch: int, capacity: int):
+        c, dev, bf = model.config, model.device, torch.bfloat16
+        self.x = torch.empty((batch, c.hidden_size), dtype=bf, device=dev)
+        self.qkv = torch.empty((batch, model.qkv_rows), dtype=bf, device=dev)
+        self.q = torch.empty((batch, c.num_attention_heads, 1, c.head_dim), dtype=bf, device=dev)
+        self.attn = torch.empty((batch, model.q_rows), dtype=bf, device=dev)
+        self.act = torch.empty((batch, c.intermediate_size), dtype=bf, device=dev)
+        self.logits = torch.empty((batch, c.vocab_size), dtype=torch.float32, device=dev)
+        parts = int(nat.load().ipe_lm_head_parts(c.vocab_size))
+        self.parts = parts
+        self.partials = torch.empty((parts, batch, nat.PARTIAL_WORDS), dtype=torch.float32, device=dev)
+        ws = int(nat.load().ipe_decode_attention_workspace(batch, c.num_attention_heads, capacity))
+        self.workspace = torch.empty(ws, dtype=torch.uint8, device=dev)
+        self.state = torch.zeros(nat.STATE_WORDS, dtype=torch.int64, device=dev)
+        self.tokens = torch.zeros(batch, dtype=torch.int64, device=dev)
+
+
+def decode_layer(model: PackedModel, index: int, buf: DecodeBuffers, k_layer: torch.Tensor, v_layer: torch.Tensor,
+                 batch: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor, stream: int) -> None:
+    """One decoder layer for one token per row at the position in the device step state
+    (src/ipe/forward.py:86-115, start > 0)."""
+    lib = nat.load()
+    c, p = model.config, model.layers[index].ptr
+    x, eps, state = buf.x.data_ptr(), c.rms_norm_eps, buf.state.data_ptr()
+    nat.check(lib.ipe_rmsnorm_qkv(x, p["in_norm"], p["w_qkv"], buf.qkv.data_ptr(), batch, c.hidden_size,
+                                  model.qkv_rows, eps, stream), "ipe_rmsnorm_qkv")
+    nat.check(lib.ipe_qk_norm_rope_append(buf.qkv.data_ptr(), batch, 1, c.num_attention_heads, c.num_key_value_heads,
+                                          p["q_norm"], p["k_norm"], cos.data_ptr(), sin.data_ptr(), 0, state,
+                                          buf.q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), capacity, eps,
+                                          stream), "ipe_qk_norm_rope_append")
+    nat.check(lib.ipe_decode_attention(buf.q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), buf.attn.data_ptr(),
+                                       batch, c.num_attention_heads, c.num_key_value_heads, capacity, 0, state,
+                                       buf.workspace.data_ptr(), buf.workspace.numel(), stream),
+              "ipe_decode_attention")
+    nat.check(lib.ipe_linear_residual(buf.attn.data_ptr(), p["w_o"], x, batch, model.q_rows, c.hidden_size, stream),
+              "ipe_linear_residual o_proj")
+    nat.check(lib.ipe_rmsnorm_gate_up_silu(x, p["post_norm"], p["w_gate_up"], buf.act.data_ptr(), batch,
+                                           c.hidden_size, c.intermediate_size, eps, stream),
+              "ipe_rmsnorm_gate_up_silu")
+    nat.check(lib.ipe_linear_residual(buf.act.data_ptr(), p["w_down"], x, batch, c.intermediate_size, c.hidden_size,
+                                      stream), "ipe_linear_residual down_proj")
