@@ -146,6 +146,24 @@ int ipe_decode_attention(const void* q, const void* k_cache, const void* v_cache
                          void* stream);
 size_t ipe_decode_attention_workspace(int batch, int q_heads, int capacity);
 
+/* The same decode attention for callers that cannot allocate device memory: a host that gives a
+ * plugin only its input and output buffers and keeps every other allocation to itself, or a loop
+ * that must not call cudaMalloc / cudaFree because they can synchronise the device. It takes no
+ * workspace and allocates nothing: the split partials go to a 2 MiB array the library declares
+ * in device memory, which every GPU that loads the library holds until the process exits.
+ * Limit: ipe_decode_attention_workspace(batch, q_heads, capacity) must be <= 2 MiB (for 16 query
+ * heads: batch x capacity up to about 8,000 positions), else IPE_ERR_UNSUPPORTED and nothing runs.
+ * The first call on each device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current); make that first call before any stream capture. All calls share the one
+ * array and it keeps the last call's contents; nothing in it needs clearing, because a call only
+ * reads the partial records it wrote itself. Calls whose executions overlap on the GPU (other
+ * streams, other threads) race on the array and must be serialised by the caller.
+ * No counterpart in the reference: this entry point exists only in this library. */
+int ipe_decode_attention_static_scratch(const void* q, const void* k_cache, const void* v_cache,
+                                        void* out, int batch, int q_heads, int kv_heads,
+                                        int capacity, int length, const int64_t* state,
+                                        void* stream);
+
 /* Causal flash-attention over a prompt of `tokens` positions written at cache positions
  * 0..tokens-1.
  *   q bf16 [batch, q_heads, tokens, 128] -> out bf16 [batch, tokens, q_heads * 128]

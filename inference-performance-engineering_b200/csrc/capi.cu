@@ -51,6 +51,11 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
 }  // namespace
 
+namespace ipe {
+// Lets entry points defined in other files set the calling thread's ipe_last_error() message.
+int report_failure(int status, const char* message) { return fail(status, "%s", message); }
+}  // namespace ipe
+
 extern "C" {
 
 const char* ipe_last_error(void) { return g_message; }

@@ -38,6 +38,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_sample_logits": (c_int, [_P, c_int64, c_int, c_float, c_uint64, _P, _P, _P]),
     "ipe_decode_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P, c_size_t, _P]),
     "ipe_decode_attention_workspace": (c_size_t, [c_int, c_int, c_int]),
+    "ipe_decode_attention_static_scratch": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P]),
     "ipe_prefill_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
     "ipe_gemm": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P]),
     "ipe_state_set": (c_int, [_P, c_int, c_int64, _P]),
