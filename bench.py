@@ -16,6 +16,7 @@ engine in oracle/, bf16, all host threads) on a bounded sample of the same workl
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -136,9 +137,11 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     from ipe_b200.synthetic import random_model
 
     batch, prompt, new, capacity, temperature = WORKLOADS[args.workload]
+    new = args.new_tokens or new
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(device)
-    loaded = random_model(QWEN3_1_7B, seed=0, device=device, generator_device=device)
+    config = QWEN3_1_7B if not args.layers else dataclasses.replace(QWEN3_1_7B, num_hidden_layers=args.layers)
+    loaded = random_model(config, seed=0, device=device, generator_device=device)
     engine = Engine(loaded, batch=batch, capacity=capacity)
     ids_host = torch.randint(0, QWEN3_1_7B.vocab_size, (batch, prompt), generator=torch.Generator().manual_seed(0))
     ids_dev = ids_host.to(device)
@@ -196,7 +199,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     decode_tokens = world * batch * (new - 1) * steps
     value = decode_tokens / decode_s
     context = prompt + (new - 1) / 2
-    step_bytes = decode_bytes_per_step(QWEN3_1_7B, batch, context)
+    step_bytes = decode_bytes_per_step(config, batch, context)
     decode_gbs = step_bytes * (new - 1) * steps / decode_s / 1e9  # per GPU
     achieved = kernel["bytes"] / kernel["seconds"] / 1e9
     launches = engine.kernel_launches(prompt, new)
@@ -208,7 +211,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
         "config": {"workload": f"{args.workload}: Qwen3-1.7B arch bf16, batch {batch}, prompt {prompt}, "
                                f"{new} new tokens, capacity {capacity}, temperature {temperature}",
                    "batch_per_gpu": batch, "prompt": prompt, "new_tokens": new, "capacity": capacity,
-                   "parallelism": f"dp{world} (independent replicas)",
+                   "parallelism": f"dp{world} (independent replicas)", "layers": config.num_hidden_layers,
                    "l2": "weights 3.44 GB per step > 126 MB L2 (no flush needed)"},
         "prefill_tok_s": round(world * batch * prompt * steps / prefill_s, 1),
         "decode_ms_per_token": round(decode_s / ((new - 1) * steps) * 1e3, 4),
@@ -305,6 +308,8 @@ def main() -> None:
     parser.add_argument("--impl", default="ours", choices=("ours", "reference"))
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--cpu-decode-steps", type=int, default=8)
+    parser.add_argument("--new-tokens", type=int, default=0, help="override the workload's new tokens (profiling)")
+    parser.add_argument("--layers", type=int, default=0, help="fewer decoder layers (profiling only; not a bench line)")
     args = parser.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
