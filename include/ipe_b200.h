@@ -89,31 +89,48 @@ int ipe_qk_norm_rope_append(const void* qkv, int batch, int tokens, int q_heads,
                             int capacity, float eps, void* stream);
 
 /* ------------------------------------------------------------------ decode linear layers
- * Weight-streaming kernels for batch 1..16 rows (one token each). Weights bf16 [out, in]. */
+ * Weight-streaming kernels for batch 1..16 rows (one token each). Their weight operand is the
+ * "decode tile" layout of a bf16 [out, in] matrix (out % 32 == 0, in % 128 == 0), built once by
+ * ipe_decode_tiles: 8 KB tiles of 32 rows x 128 columns (for gate/up: 16 gate rows then the 16
+ * matching up rows), 16-byte chunks swizzled, row-block-major, so every weight byte is streamed by
+ * one contiguous bulk copy. One persistent CTA per SM streams its share of the tiles through a
+ * shared-memory ring; when the reduction dimension is split across CTAs, partial tiles go to
+ * `workspace` (ipe_decode_linear_workspace bytes, zero-filled before its first use; the kernels
+ * leave its counters at zero, so one workspace serves every call on a stream). Launched with
+ * programmatic dependent launch: a call's weight stream overlaps the end of the previous kernel. */
 
-/* qkv[b,:] = rms_norm(x[b,:]) @ w_qkv^T; w_qkv rows are q_proj | k_proj | v_proj.
+/* Writes the decode tiles of w [rows, in] (or, with w_up, of the gate/up pair w = gate_proj,
+ * w_up = up_proj, each [rows, in]) into `tiles` (ipe_decode_tiles_bytes bytes). */
+int ipe_decode_tiles(const void* w, const void* w_up, void* tiles, int rows, int in_features,
+                     void* stream);
+size_t ipe_decode_tiles_bytes(int rows, int in_features, int gate_up_pair);
+size_t ipe_decode_linear_workspace(int batch, int weight_rows, int in_features);
+
+/* qkv[b,:] = rms_norm(x[b,:]) @ w_qkv^T; w_qkv (decode tiles) rows are q_proj | k_proj | v_proj.
  * Replaces src/ipe/forward.py:100-103 (rms_norm + three F.linear). */
 int ipe_rmsnorm_qkv(const void* x, const void* norm_weight, const void* w_qkv, void* qkv_out,
-                    int batch, int hidden, int qkv_rows, float eps, void* stream);
+                    int batch, int hidden, int qkv_rows, float eps, void* workspace,
+                    size_t workspace_bytes, void* stream);
 
 /* x[b,n] = bf16(x[b,n] + bf16(a[b,:] . w[n,:])). Replaces the o_proj and down_proj residual
  * updates, src/ipe/forward.py:113 and :115. */
 int ipe_linear_residual(const void* a, const void* w, void* x, int batch, int in_features,
-                        int out_features, void* stream);
+                        int out_features, void* workspace, size_t workspace_bytes, void* stream);
 
 /* act[b,j] = bf16(bf16(silu(bf16(g))) * bf16(u)), g / u = rms_norm(x[b]) . gate/up row j;
- * w_gate_up packed in IPE_GATE_UP_GROUP row groups. Replaces src/ipe/forward.py:114-115
+ * w_gate_up: the decode tiles of the (gate_proj, up_proj) pair. Replaces src/ipe/forward.py:114-115
  * (rms_norm, then ops.swiglu's gate/up/silu/mul, src/ipe/ops.py:104-106). */
 int ipe_rmsnorm_gate_up_silu(const void* x, const void* norm_weight, const void* w_gate_up,
                              void* act_out, int batch, int hidden, int intermediate, float eps,
-                             void* stream);
+                             void* workspace, size_t workspace_bytes, void* stream);
 
-/* Final RMSNorm of x rows (row b at x + b*x_row_stride elements), tied LM head, fp32 logits
+/* Final RMSNorm of x rows (row b at x + b*x_row_stride elements), tied LM head (its decode
+ * tiles), fp32 logits
  * (bf16-rounded then widened, as the reference), and per-block sampling partials
  * [ipe_lm_head_parts(vocab)][batch][IPE_PARTIAL_WORDS] for ipe_sample. temperature > 0 adds
  * Gumbel noise from (seed, position) to the sampling partials only.
  * Replaces src/ipe/engine.py:110-111 and the first pass of src/ipe/engine.py:28-41. */
-int ipe_lm_head(const void* x, int64_t x_row_stride, const void* norm_weight, const void* embed,
+int ipe_lm_head(const void* x, int64_t x_row_stride, const void* norm_weight, const void* embed_tiles,
                 float* logits, float* partials, int batch, int hidden, int vocab, float eps,
                 float temperature, uint64_t seed, const int64_t* state, void* stream);
 int ipe_lm_head_parts(int vocab);
@@ -145,6 +162,21 @@ int ipe_decode_attention(const void* q, const void* k_cache, const void* v_cache
                          const int64_t* state, void* workspace, size_t workspace_bytes,
                          void* stream);
 size_t ipe_decode_attention_workspace(int batch, int q_heads, int capacity);
+
+/* One decode step's attention straight from the QKV projection output: per-head q_norm / k_norm
+ * and RoPE of the step's query and key (as ipe_qk_norm_rope_append), the K/V append at position
+ * `start` (state[IPE_STATE_POS] when state is non-null), split-KV attention over positions
+ * 0..position, and the merge of the chunks by the last chunk block of each (row, KV head).
+ *   qkv bf16 [batch, (q_heads + 2*kv_heads) * 128] -> out bf16 [batch, q_heads * 128]
+ * workspace: ipe_decode_attention_qkv_workspace bytes, zero-filled before first use (its arrival
+ * counters return to zero after every call). Replaces src/ipe/forward.py:101-112 for a decode step
+ * (qk_norm, apply_rotary, cache write, ops.attention). */
+int ipe_decode_attention_qkv(const void* qkv, const void* q_norm_weight, const void* k_norm_weight,
+                             const void* cos_table, const void* sin_table, int start,
+                             const int64_t* state, void* k_cache, void* v_cache, void* out, int batch,
+                             int q_heads, int kv_heads, int capacity, float eps, void* workspace,
+                             size_t workspace_bytes, void* stream);
+size_t ipe_decode_attention_qkv_workspace(int batch, int q_heads, int kv_heads, int capacity);
 
 /* The same decode attention for callers that cannot allocate device memory: a host that gives a
  * plugin only its input and output buffers and keeps every other allocation to itself, or a loop

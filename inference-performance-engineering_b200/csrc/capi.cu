@@ -118,42 +118,80 @@ int ipe_qk_norm_rope_append(const void* qkv, int batch, int tokens, int q_heads,
 static int gemv_checks(const char* name, const void* x, const void* w, const void* out, int batch, int k, int rows) {
   if (!x || !w || !out) return fail(IPE_ERR_ARGUMENT, "%s: null pointer", name);
   if (batch < 1 || batch > 16) return fail(IPE_ERR_UNSUPPORTED, "%s: batch %d outside 1..16", name, batch);
-  if (k < 32 || k % 32) return fail(IPE_ERR_UNSUPPORTED, "%s: in_features %d is not a multiple of 32", name, k);
+  if (k < 128 || k % 128) return fail(IPE_ERR_UNSUPPORTED, "%s: in_features %d is not a multiple of 128", name, k);
   if (rows < 1) return fail(IPE_ERR_ARGUMENT, "%s: out_features %d", name, rows);
+  if (rows % 32) return fail(IPE_ERR_UNSUPPORTED, "%s: out_features %d is not a multiple of 32", name, rows);
   if (!aligned16(x) || !aligned16(w)) return fail(IPE_ERR_ARGUMENT, "%s: operands must be 16-byte aligned", name);
   return IPE_OK;
 }
 
-static int run_gemv(const char* name, ipe::GemvArgs a, cudaStream_t stream) {
+static int run_gemv(const char* name, ipe::GemvArgs a, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   a.err = device_error_word();
-  if (ipe::gemv_smem_bytes(a) > 227 * 1024)
-    return fail(IPE_ERR_UNSUPPORTED, "%s: batch %d x width %d does not fit in shared memory", name, a.batch, a.k);
-  return cuda_status(ipe::launch_gemv(a, stream), name);
+  const size_t need = ipe::gemv_workspace_bytes(a);
+  if (need && (!workspace || workspace_bytes < need))
+    return fail(IPE_ERR_ARGUMENT, "%s: a zero-filled workspace of %zu bytes is needed", name, need);
+  const char* message = nullptr;
+  cudaError_t e = ipe::launch_gemv(a, workspace, stream, &message);
+  if (e != cudaSuccess && message) return fail(IPE_ERR_CUDA, "%s: %s", name, message);
+  return cuda_status(e, name);
+}
+
+size_t ipe_decode_tiles_bytes(int rows, int in_features, int gate_up_pair) {
+  if (rows < 1 || in_features < 128 || in_features % 128) return 0;
+  return ipe::decode_tiles_bytes(rows, in_features, gate_up_pair != 0);
+}
+
+int ipe_decode_tiles(const void* w, const void* w_up, void* tiles, int rows, int in_features, void* stream) {
+  if (!w || !tiles) return fail(IPE_ERR_ARGUMENT, "ipe_decode_tiles: null pointer");
+  if (rows < 1 || in_features < 128 || in_features % 128)
+    return fail(IPE_ERR_UNSUPPORTED, "ipe_decode_tiles: in_features %d is not a multiple of 128", in_features);
+  if (w_up ? rows % 16 : rows % 32)
+    return fail(IPE_ERR_UNSUPPORTED, "ipe_decode_tiles: rows %d must be a multiple of %d", rows, w_up ? 16 : 32);
+  if (!aligned16(w) || !aligned16(tiles) || (w_up && !aligned16(w_up)))
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_tiles: pointers must be 16-byte aligned");
+  return cuda_status(ipe::launch_decode_tiles(w, w_up, tiles, rows, in_features, as_stream(stream)),
+                     "ipe_decode_tiles");
+}
+
+size_t ipe_decode_linear_workspace(int batch, int weight_rows, int in_features) {
+  if (batch < 1 || batch > 16 || weight_rows < 1 || in_features < 128 || in_features % 128) return 0;
+  ipe::GemvArgs a{};
+  a.batch = batch;
+  a.rows = weight_rows;
+  a.k = in_features;
+  size_t most = 0;
+  for (int epi : {ipe::kGemvStore, ipe::kGemvSiluMul}) {
+    a.epilogue = epi;
+    const size_t need = ipe::gemv_workspace_bytes(a);
+    if (need > most) most = need;
+  }
+  return most;
 }
 
 int ipe_rmsnorm_qkv(const void* x, const void* norm_weight, const void* w_qkv, void* qkv_out, int batch, int hidden,
-                    int qkv_rows, float eps, void* stream) {
+                    int qkv_rows, float eps, void* workspace, size_t workspace_bytes, void* stream) {
   int s = gemv_checks("ipe_rmsnorm_qkv", x, w_qkv, qkv_out, batch, hidden, qkv_rows);
   if (s) return s;
   if (!norm_weight || !aligned16(norm_weight)) return fail(IPE_ERR_ARGUMENT, "ipe_rmsnorm_qkv: norm_weight");
   ipe::GemvArgs a{};
   a.x = x; a.x_stride = hidden; a.norm_weight = norm_weight; a.eps = eps; a.w = w_qkv; a.rows = qkv_rows; a.k = hidden;
   a.batch = batch; a.out = qkv_out; a.out_stride = qkv_rows; a.epilogue = ipe::kGemvStore;
-  return run_gemv("ipe_rmsnorm_qkv", a, as_stream(stream));
+  return run_gemv("ipe_rmsnorm_qkv", a, workspace, workspace_bytes, as_stream(stream));
 }
 
 int ipe_linear_residual(const void* act, const void* w, void* x, int batch, int in_features, int out_features,
-                        void* stream) {
+                        void* workspace, size_t workspace_bytes, void* stream) {
   int s = gemv_checks("ipe_linear_residual", act, w, x, batch, in_features, out_features);
   if (s) return s;
   ipe::GemvArgs a{};
   a.x = act; a.x_stride = in_features; a.w = w; a.rows = out_features; a.k = in_features; a.batch = batch;
   a.out = x; a.out_stride = out_features; a.epilogue = ipe::kGemvResidual;
-  return run_gemv("ipe_linear_residual", a, as_stream(stream));
+  return run_gemv("ipe_linear_residual", a, workspace, workspace_bytes, as_stream(stream));
 }
 
 int ipe_rmsnorm_gate_up_silu(const void* x, const void* norm_weight, const void* w_gate_up, void* act_out, int batch,
-                             int hidden, int intermediate, float eps, void* stream) {
+                             int hidden, int intermediate, float eps, void* workspace, size_t workspace_bytes,
+                             void* stream) {
   int s = gemv_checks("ipe_rmsnorm_gate_up_silu", x, w_gate_up, act_out, batch, hidden, 2 * intermediate);
   if (s) return s;
   if (intermediate % IPE_GATE_UP_GROUP)
@@ -163,7 +201,7 @@ int ipe_rmsnorm_gate_up_silu(const void* x, const void* norm_weight, const void*
   ipe::GemvArgs a{};
   a.x = x; a.x_stride = hidden; a.norm_weight = norm_weight; a.eps = eps; a.w = w_gate_up; a.rows = 2 * intermediate;
   a.k = hidden; a.batch = batch; a.out = act_out; a.out_stride = intermediate; a.epilogue = ipe::kGemvSiluMul;
-  return run_gemv("ipe_rmsnorm_gate_up_silu", a, as_stream(stream));
+  return run_gemv("ipe_rmsnorm_gate_up_silu", a, workspace, workspace_bytes, as_stream(stream));
 }
 
 int ipe_lm_head_parts(int vocab) { return vocab < 1 ? 0 : (vocab + 31) / 32; }
@@ -180,7 +218,7 @@ int ipe_lm_head(const void* x, int64_t x_row_stride, const void* norm_weight, co
   a.x = x; a.x_stride = x_row_stride; a.norm_weight = norm_weight; a.eps = eps; a.w = embed; a.rows = vocab;
   a.k = hidden; a.batch = batch; a.out = logits; a.out_stride = vocab; a.partials = partials;
   a.temperature = temperature; a.seed = seed; a.state = state; a.epilogue = ipe::kGemvLogits;
-  return run_gemv("ipe_lm_head", a, as_stream(stream));
+  return run_gemv("ipe_lm_head", a, nullptr, 0, as_stream(stream));
 }
 
 int ipe_sample(const float* partials, const float* logits, int batch, int vocab, float temperature, int64_t* state,
@@ -234,6 +272,31 @@ int ipe_decode_attention(const void* q, const void* k_cache, const void* v_cache
   return cuda_status(ipe::launch_decode_attention(q, k_cache, v_cache, out, batch, q_heads, kv_heads, capacity, length,
                                                   state, static_cast<float*>(workspace), as_stream(stream)),
                      "ipe_decode_attention");
+}
+
+size_t ipe_decode_attention_qkv_workspace(int batch, int q_heads, int kv_heads, int capacity) {
+  if (batch < 1 || q_heads < 1 || kv_heads < 1 || capacity < 1) return 0;
+  return ipe::fused_decode_workspace_bytes(batch, q_heads, kv_heads, capacity);
+}
+
+int ipe_decode_attention_qkv(const void* qkv, const void* q_norm_weight, const void* k_norm_weight,
+                             const void* cos_table, const void* sin_table, int start, const int64_t* state,
+                             void* k_cache, void* v_cache, void* out, int batch, int q_heads, int kv_heads,
+                             int capacity, float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  int s = attention_checks("ipe_decode_attention_qkv", qkv, k_cache, v_cache, out, batch, q_heads, kv_heads, capacity);
+  if (s) return s;
+  if (!q_norm_weight || !k_norm_weight || !cos_table || !sin_table)
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_attention_qkv: null pointer");
+  if (!state && (start < 0 || start >= capacity))
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_attention_qkv: position %d outside 0..%d", start, capacity - 1);
+  const size_t need = ipe::fused_decode_workspace_bytes(batch, q_heads, kv_heads, capacity);
+  if (!workspace || workspace_bytes < need)
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_attention_qkv: a zero-filled workspace of %zu bytes is needed", need);
+  return cuda_status(ipe::launch_decode_attention_fused(qkv, q_norm_weight, k_norm_weight, cos_table, sin_table, state,
+                                                        start, k_cache, v_cache, out, batch, q_heads, kv_heads,
+                                                        capacity, eps, workspace, device_error_word(),
+                                                        as_stream(stream)),
+                     "ipe_decode_attention_qkv");
 }
 
 int ipe_prefill_attention(const void* q, const void* k_cache, const void* v_cache, void* out, int batch, int q_heads,

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "ipe_b200.h"
 
 #ifndef __CUDACC__
@@ -62,8 +64,20 @@ __device__ __forceinline__ uint4 ldg_stream(const void* p) {
   return v;
 }
 
+// Read-only-path load: only for data no kernel writes while this one may run (weights, tables).
 __device__ __forceinline__ uint4 ldg16(const void* p) {
   return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+// L2-only load for data an earlier kernel wrote. Under programmatic dependent launch a kernel's
+// CTAs can be resident while its predecessor still writes, so L1 lines filled meanwhile could be
+// stale; .cg reads bypass L1.
+__device__ __forceinline__ uint4 ldcg16(const void* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ uint2 ldcg8(const void* p) { return __ldcg(reinterpret_cast<const uint2*>(p)); }
+__device__ __forceinline__ float ldcg_bf16(const bf16* p) {
+  return __uint_as_float(static_cast<uint32_t>(__ldcg(reinterpret_cast<const unsigned short*>(p))) << 16);
 }
 
 template <typename T>
@@ -87,6 +101,31 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 
 // Wall-clock bound of every spin-wait in these kernels.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+// ------------------------------------------------------------- programmatic dependent launch
+// Kernels launched with launch_pdl may start while the previous kernel in the stream is still
+// running. Before pdl_wait() they may only touch data no earlier kernel writes (the weights);
+// pdl_wait() returns once every earlier kernel has completed and its writes are visible.
+// pdl_trigger() lets the next kernel start launching its CTAs.
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = grid;
+  config.blockDim = block;
+  config.dynamicSmemBytes = smem;
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attribute[0].val.programmaticStreamSerializationAllowed = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  return cudaLaunchKernelEx(&config, kernel, std::forward<Args>(args)...);
+}
 
 // ------------------------------------------------------------------------- mbarrier helpers
 
@@ -124,6 +163,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_addr(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+// 2-D TMA tile load into this CTA's shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(x), "r"(y)
+      : "memory");
 }
 
 // Bounded wait: returns false (and reports) if the phase did not complete within the limit.

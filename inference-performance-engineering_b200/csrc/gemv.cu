@@ -1,20 +1,46 @@
-// Decode linear layers: weight-streaming GEMV for 1..16 activation rows on the tensor pipe.
+// Decode linear layers: persistent, bulk-copy-fed weight-streaming GEMV for 1..16 activation rows.
 //
-// Each CTA owns 16 (or 32) weight rows and the whole reduction dimension; its 8 warps split K in
-// 32-wide chunks. A thread streams 16-byte pieces of two weight rows with L1-bypassing loads and
-// feeds them to mma.sync m16n8k16 as the A operand; the activations are the B operand. The MMA's
-// K order is permuted the same way for A and B (physical k = 8*tig + j), which keeps every weight
-// load a contiguous 16 bytes while the dot product is unchanged. Per-warp partial tiles are
-// summed through shared memory and the epilogue applies the reference's rounding points.
+// Weight layout ("decode tiles", built once by ipe_decode_tiles): a row block of 32 output rows
+// (for SiLU*up: 16 gate rows then the 16 matching up rows) and 128 columns form one contiguous
+// 8 KB tile: [half (2)][64-column box (2)][row (16)][128 bytes], each 128-byte row segment stored
+// with its 16-byte chunks XOR-swizzled by (row % 8). Tiles run row-block-major, so a row block's
+// K range is one contiguous span of memory.
+//
+// Work: each row block's K range is split into `ksplit` pieces; pieces are dealt in contiguous
+// ranges to one CTA per SM, and within a CTA round-robin to its 4 consumer warps. One producer
+// thread streams the CTA's tiles with 8 KB cp.async.bulk copies into shared-memory slots
+// (mbarrier full/empty pairs), 3 slots owned by each consumer warp, so ~96 KB of weights are in
+// flight per SM. A slot has exactly one consumer, which waits for its fills in order: a parity
+// wait is then never more than one phase ahead of the barrier (a shared ring would let a fast
+// warp wait two phases ahead, where the parity aliases). Activations
+// (normalised once per CTA for the norm-fused layers) sit in shared memory; consumer warps read
+// their slot with conflict-free 16-byte loads and feed mma.sync m16n8k16 (weights = A,
+// activations = B, the same K permutation on both sides so every read is a contiguous 16 bytes).
+// With ksplit > 1, pieces write fp32 partial tiles to the workspace and the last piece of a row
+// block to arrive (an atomic counter) sums them in piece order - deterministic - applies the
+// epilogue with the reference's rounding points and resets the counter.
+//
+// Launched with programmatic dependent launch: the producer streams weights before the previous
+// kernel has finished; consumers wait (griddepcontrol.wait) before reading activations.
 #include "common.cuh"
 #include "launch.h"
+#include "sampling.cuh"
+#include "tensor_map.h"
 
 namespace ipe {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
-constexpr int kPadElems = 32;  // 64-byte pad per staged activation row: conflict-free 16-byte reads
+constexpr int kConsumers = 4;
+constexpr int kSlotsPerWarp = 3;
+constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kTileBytes = 8192;  // 32 rows x 128 bf16
+constexpr int kBoxBytes = 2048;   // 16 rows x 64 bf16
+constexpr int kSubK = 128;
+constexpr int kMaxStages = kConsumers * kSlotsPerWarp;
+constexpr int kPad = 32;  // bf16 elements of padding per staged activation row
+constexpr size_t kCounterBytes = 32768;  // arrival counters for up to 8192 row blocks
+constexpr size_t kSmemLimit = 200 * 1024;
+constexpr size_t kFixedSmem = 1024 + 2 * kMaxStages * 8 + 16 * 4 + 64;
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -25,400 +51,447 @@ __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// Philox4x32-10 (Salmon et al., "Parallel random numbers: as easy as 1, 2, 3", SC'11): first word.
-__device__ __forceinline__ uint32_t philox_word(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, uint32_t k0,
-                                                uint32_t k1) {
-#pragma unroll
-  for (int r = 0; r < 10; ++r) {
-    const uint32_t hi0 = __umulhi(0xD2511F53u, c0), lo0 = 0xD2511F53u * c0;
-    const uint32_t hi1 = __umulhi(0xCD9E8D57u, c2), lo1 = 0xCD9E8D57u * c2;
-    c0 = hi1 ^ c1 ^ k0;
-    c1 = lo1;
-    c2 = hi0 ^ c3 ^ k1;
-    c3 = lo0;
-    k0 += 0x9E3779B9u;
-    k1 += 0xBB67AE85u;
-  }
-  return c0;
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
 }
 
-// Uniform on [0, 1) with 24 random bits, for (vocab id, batch row, sampled-token index).
-__device__ __forceinline__ float uniform01(uint64_t seed, int n, int b, int64_t step) {
-  const uint32_t r = philox_word(static_cast<uint32_t>(n), static_cast<uint32_t>(b), static_cast<uint32_t>(step),
-                                 static_cast<uint32_t>(step >> 32), static_cast<uint32_t>(seed),
-                                 static_cast<uint32_t>(seed >> 32));
-  return static_cast<float>(r >> 8) * (1.0f / 16777216.0f);
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <int RT, int EPI>
-__device__ __forceinline__ int weight_row(int block, int rt, int r) {
-  if constexpr (EPI == kGemvSiluMul) {
-    // 16 intermediate rows j0..j0+15 per block: gate rows, then the matching up rows.
-    const int j0 = block * 16;
-    return (j0 / IPE_GATE_UP_GROUP) * (2 * IPE_GATE_UP_GROUP) + (j0 % IPE_GATE_UP_GROUP) + rt * IPE_GATE_UP_GROUP + r;
-  } else {
-    return block * 16 * RT + rt * 16 + r;
-  }
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
 }
 
-template <int NT, int RT, bool NORM, int EPI, int U>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const GemvArgs a) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
-  const int K = a.k, B = a.batch;
-  const bf16* __restrict__ x = static_cast<const bf16*>(a.x);
-  const bf16* __restrict__ w = static_cast<const bf16*>(a.w);
-  const int xs_stride = K + kPadElems;
-  bf16* xs = reinterpret_cast<bf16*>(smem);
-  float* red = reinterpret_cast<float*>(smem + (NORM ? static_cast<size_t>(B) * xs_stride * 2 : 0));
-  constexpr int kRows = RT * 16, kCols = NT * 8, kOut = kRows * kCols;
-  float* fin = red + kWarps * kOut;
+struct Plan {
+  int row_blocks;
+  int ksplit;
+  int piece_k;  // columns per piece, a multiple of kSubK
+  int pieces;
+  int stages;
+  int act_smem;  // activations staged in shared memory (else read from global per tile)
+  int64_t tiles;  // tiles in the weight buffer: row_blocks * (k / kSubK)
+  size_t smem;
+};
 
-  if constexpr (NORM) {
-    // Stage rms_norm(x) rows in shared memory with the reference's two roundings.
-    const bf16* __restrict__ nw = static_cast<const bf16*>(a.norm_weight);
-    for (int b = warp; b < B; b += kWarps) {
-      const bf16* xr = x + b * a.x_stride;
-      float ss = 0.f;
-      for (int c = lane; c < K / 8; c += 32) {
-        float f[8];
-        unpack8(ldg16(xr + c * 8), f);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
-      }
-      ss = warp_sum(ss);
-      const float rstd = rsqrtf(ss / static_cast<float>(K) + a.eps);
-      for (int c = lane; c < K / 8; c += 32) {
-        float f[8], wf[8], h[8];
-        unpack8(ldg16(xr + c * 8), f);
-        unpack8(ldg16(nw + c * 8), wf);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) h[i] = wf[i] * bf16_round(f[i] * rstd);
-        *reinterpret_cast<uint4*>(xs + b * xs_stride + c * 8) = pack8(h);
-      }
+template <int NT, int EPI, bool NORM, bool ACT_SMEM>
+__global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const GemvArgs a, const Plan plan) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int stages = plan.stages;
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + stages * kTileBytes);
+  uint64_t* empty = full + kMaxStages;
+  float* rstd = reinterpret_cast<float*>(empty + kMaxStages);
+  bf16* xs = reinterpret_cast<bf16*>(rstd + 16);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t G = gridDim.x;
+  const int p0 = static_cast<int>(static_cast<int64_t>(blockIdx.x) * plan.pieces / G);
+  const int p1 = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * plan.pieces / G);
+  const int npieces = p1 - p0;
+  const int subs = plan.piece_k / kSubK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
     }
-    __syncthreads();
-  }
-
-  int rows_idx[RT][2];
-  bool rows_ok[RT][2];
-#pragma unroll
-  for (int rt = 0; rt < RT; ++rt) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = weight_row<RT, EPI>(blockIdx.x, rt, g + 8 * h);
-      rows_ok[rt][h] = r < a.rows;
-      rows_idx[rt][h] = rows_ok[rt][h] ? r : 0;
-    }
-  }
-
-  float acc[RT][NT][4];
-#pragma unroll
-  for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[rt][j][i] = 0.f;
-
-  const int chunks = K / 32;
-  for (int c0 = warp; c0 < chunks; c0 += kWarps * U) {
-    uint4 wv[U][RT][2];
-    uint4 xv[U][NT];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int c = c0 + u * kWarps;
-      const bool live = c < chunks;
-      const int k = c * 32 + 8 * t;
-#pragma unroll
-      for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          wv[u][rt][h] = (live && rows_ok[rt][h]) ? ldg_stream(w + static_cast<int64_t>(rows_idx[rt][h]) * K + k)
-                                                  : make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int j = 0; j < NT; ++j) {
-        const int b = 8 * j + g;
-        if (live && b < B) {
-          if constexpr (NORM) xv[u][j] = *reinterpret_cast<const uint4*>(xs + b * xs_stride + k);
-          else xv[u][j] = ldg16(x + b * a.x_stride + k);
-        } else {
-          xv[u][j] = make_uint4(0, 0, 0, 0);
-        }
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-#pragma unroll
-      for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-        for (int j = 0; j < NT; ++j) {
-          mma16816(acc[rt][j], wv[u][rt][0].x, wv[u][rt][1].x, wv[u][rt][0].y, wv[u][rt][1].y, xv[u][j].x,
-                   xv[u][j].y);
-          mma16816(acc[rt][j], wv[u][rt][0].z, wv[u][rt][1].z, wv[u][rt][0].w, wv[u][rt][1].w, xv[u][j].z,
-                   xv[u][j].w);
-        }
-  }
-
-  // Cross-warp reduction: red[warp][row][col], col = batch row.
-#pragma unroll
-  for (int rt = 0; rt < RT; ++rt)
-#pragma unroll
-    for (int j = 0; j < NT; ++j)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int r = rt * 16 + g + 8 * (i >> 1);
-        const int col = 8 * j + 2 * t + (i & 1);
-        red[(warp * kRows + r) * kCols + col] = acc[rt][j][i];
-      }
-  __syncthreads();
-  for (int o = threadIdx.x; o < kOut; o += kThreads) {
-    float s = 0.f;
-#pragma unroll
-    for (int v = 0; v < kWarps; ++v) s += red[v * kOut + o];
-    fin[o] = s;
+    fence_barrier_init();
   }
   __syncthreads();
+  pdl_trigger();
 
-  if constexpr (EPI == kGemvStore || EPI == kGemvResidual) {
-    bf16* out = static_cast<bf16*>(a.out);
-    for (int o = threadIdx.x; o < kOut; o += kThreads) {
-      const int r = o / kCols, b = o % kCols;
-      const int n = weight_row<RT, EPI>(blockIdx.x, r / 16, r % 16);
-      if (b >= B || n >= a.rows) continue;
-      bf16* dst = out + b * a.out_stride + n;
-      if constexpr (EPI == kGemvStore) {
-        *dst = __float2bfloat16_rn(fin[o]);
-      } else {
-        *dst = __float2bfloat16_rn(__bfloat162float(*dst) + bf16_round(fin[o]));
-      }
-    }
-  } else if constexpr (EPI == kGemvSiluMul) {
-    bf16* out = static_cast<bf16*>(a.out);
-    for (int o = threadIdx.x; o < 16 * kCols; o += kThreads) {
-      const int r = o / kCols, b = o % kCols;
-      if (b >= B) continue;
-      const float gate = bf16_round(fin[r * kCols + b]);
-      const float up = bf16_round(fin[(16 + r) * kCols + b]);
-      const float act = bf16_round(gate / (1.0f + expf(-gate)));
-      out[b * a.out_stride + blockIdx.x * 16 + r] = __float2bfloat16_rn(act * up);
-    }
-  } else {  // logits + sampling partials
-    float* logits = static_cast<float*>(a.out);
-    for (int o = threadIdx.x; o < kOut; o += kThreads) {
-      const int r = o / kCols, b = o % kCols;
-      const int n = weight_row<RT, EPI>(blockIdx.x, r / 16, r % 16);
-      const float l = bf16_round(fin[o]);
-      fin[o] = l;
-      if (b < B && n < a.rows) logits[b * a.out_stride + n] = l;
-    }
-    __syncthreads();
-    if (threadIdx.x < B) {
-      const int b = threadIdx.x;
-      const int n0 = weight_row<RT, EPI>(blockIdx.x, 0, 0);
-      const int valid = min(kRows, a.rows - n0);
-      float m = -INFINITY;
-      int arg = n0;
-      for (int r = 0; r < valid; ++r) {
-        const float l = fin[r * kCols + b];
-        if (l > m) {
-          m = l;
-          arg = n0 + r;
-        }
-      }
-      float s = 0.f;
-      if (m > -INFINITY)
-        for (int r = 0; r < valid; ++r) s += expf(fin[r * kCols + b] - m);
-      float gs = -INFINITY;
-      int garg = n0;
-      const float temperature = a.state ? __int_as_float(static_cast<int>(a.state[IPE_STATE_TEMPERATURE])) : a.temperature;
-      if (temperature > 0.f) {
-        const uint64_t seed = a.state ? static_cast<uint64_t>(a.state[IPE_STATE_SEED]) : a.seed;
-        const int64_t step = a.state ? a.state[IPE_STATE_STEP] : 0;
-        for (int r = 0; r < valid; ++r) {
-          const float u = uniform01(seed, n0 + r, b, step);
-          const float score = fin[r * kCols + b] / temperature - logf(-logf(u));
-          if (score > gs) {
-            gs = score;
-            garg = n0 + r;
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (weights only)
+    if (lane == 0) {
+      // Piece p's tiles are p * subs .. p * subs + subs - 1 (a row block's pieces are adjacent), so
+      // the walk is pointer arithmetic only: the single issuing thread must stay far ahead. Warp w's
+      // k-th tile goes to its slot w * kSlotsPerWarp + k % kSlotsPerWarp as fill k / kSlotsPerWarp.
+      const unsigned char* first = static_cast<const unsigned char*>(a.w) + static_cast<int64_t>(p0) * subs * kTileBytes;
+      const uint32_t ring_base = smem_addr(ring);
+      const int64_t piece_bytes = static_cast<int64_t>(subs) * kTileBytes;
+      bool ok = true;
+      for (int q0 = 0, k0 = 0; q0 < npieces && ok; q0 += kConsumers, k0 += subs) {
+        const int gs = min(kConsumers, npieces - q0);
+        const unsigned char* group = first + q0 * piece_bytes;
+        for (int s = 0; s < subs && ok; ++s) {
+          const int k = k0 + s;
+          const int fill = k / kSlotsPerWarp, sub = k - fill * kSlotsPerWarp;
+          const unsigned char* src = group + s * kTileBytes;
+          for (int w = 0; w < gs; ++w, src += piece_bytes) {
+            const int64_t tile = static_cast<int64_t>(p0 + q0 + w) * subs + s;
+            if (tile < 0 || tile >= plan.tiles) {  // never expected: refuse the copy, report
+              report(a.err, kErrShape);
+              ok = false;
+              break;
+            }
+            const int slot = w * kSlotsPerWarp + sub;
+            if (fill > 0 && !mbar_wait(&empty[slot], (fill - 1) & 1, a.err)) {
+              ok = false;
+              break;
+            }
+            mbar_expect_tx(&full[slot], kTileBytes);
+            bulk_copy(ring_base + slot * kTileBytes, src, kTileBytes, &full[slot]);
           }
         }
       }
-      float* rec = a.partials + (static_cast<int64_t>(blockIdx.x) * B + b) * IPE_PARTIAL_WORDS;
-      rec[0] = m;
-      rec[1] = s;
-      rec[2] = gs;
-      rec[3] = 0.f;
-      rec[4] = __int_as_float(arg);
-      rec[5] = __int_as_float(garg);
+    }
+    return;
+  }
+
+  // ------------------------------------------------------------------ consumers
+  const int cw = warp - 1;
+  const int g = lane >> 2, t = lane & 3;
+  const int B = a.batch, K = a.k;
+  const int xs_stride = K + kPad;
+  const bf16* __restrict__ x = static_cast<const bf16*>(a.x);
+  const bf16* __restrict__ nw = static_cast<const bf16*>(a.norm_weight);
+  pdl_wait();
+  if constexpr (NORM || ACT_SMEM) {
+    for (int b = cw; b < B; b += kConsumers) {
+      const bf16* xr = x + b * a.x_stride;
+      float r = 1.f;
+      if constexpr (NORM) {
+        float ss = 0.f;
+        for (int c = lane; c < K / 8; c += 32) {
+          float f[8];
+          unpack8(ldcg16(xr + c * 8), f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+        }
+        ss = warp_sum(ss);
+        r = rsqrtf(ss / static_cast<float>(K) + a.eps);
+        if (lane == 0) rstd[b] = r;
+      }
+      if constexpr (ACT_SMEM) {
+        for (int c = lane; c < K / 8; c += 32) {
+          uint4 v = ldcg16(xr + c * 8);
+          if constexpr (NORM) {
+            float f[8], wf[8];
+            unpack8(v, f);
+            unpack8(ldg16(nw + c * 8), wf);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * r);
+            v = pack8(f);
+          }
+          *reinterpret_cast<uint4*>(xs + b * xs_stride + c * 8) = v;
+        }
+      }
+    }
+    named_barrier(1, kConsumers * 32);
+  }
+  float my_rstd[NT];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) my_rstd[j] = (NORM && !ACT_SMEM && 8 * j + g < B) ? rstd[8 * j + g] : 0.f;
+
+  for (int q = 0; q * kConsumers < npieces; ++q) {
+    const int gs = min(kConsumers, npieces - q * kConsumers);
+    if (cw >= gs) continue;
+    const int piece = p0 + q * kConsumers + cw;
+    const int rb = piece / plan.ksplit, ks = piece % plan.ksplit;
+    float acc[2][NT][4];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0.f;
+    bool ok = true;
+    for (int s = 0; s < subs; ++s) {
+      const int k = q * subs + s;  // this warp's k-th tile
+      const int fill = k / kSlotsPerWarp;
+      const int slot = cw * kSlotsPerWarp + (k - fill * kSlotsPerWarp);
+      const int k0 = ks * plan.piece_k + s * kSubK;
+      uint4 xv[4][NT];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) {
+          const int b = 8 * j + g;
+          const int k = k0 + c * 32 + 8 * t;
+          if (b >= B) {
+            xv[c][j] = make_uint4(0, 0, 0, 0);
+          } else if constexpr (ACT_SMEM) {
+            xv[c][j] = *reinterpret_cast<const uint4*>(xs + b * xs_stride + k);
+          } else {
+            const uint4 raw = ldcg16(x + b * a.x_stride + k);
+            if constexpr (NORM) {
+              float f[8], wf[8];
+              unpack8(raw, f);
+              unpack8(ldg16(nw + k), wf);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * my_rstd[j]);
+              xv[c][j] = pack8(f);
+            } else {
+              xv[c][j] = raw;
+            }
+          }
+        }
+      if (!mbar_wait(&full[slot], fill & 1, a.err)) {
+        ok = false;
+        break;
+      }
+      const uint32_t base = smem_addr(ring + slot * kTileBytes);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        // 32-column chunk c lives in box (h, c / 2); its 16-byte piece t is logical chunk
+        // (c % 2) * 4 + t of the 128-byte row, stored at that index XOR (row % 8).
+        const int chunk = (c & 1) * 4 + t;
+        uint4 w[2][2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const int row = g + 8 * r;
+            w[h][r] = lds128(base + (h * 2 + (c >> 1)) * kBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+          }
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            mma16816(acc[h][j], w[h][0].x, w[h][1].x, w[h][0].y, w[h][1].y, xv[c][j].x, xv[c][j].y);
+            mma16816(acc[h][j], w[h][0].z, w[h][1].z, w[h][0].w, w[h][1].w, xv[c][j].z, xv[c][j].w);
+          }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+    }
+    if (!ok) break;
+
+    // ---------------------------------------------------------------- split-K reduction
+    if (plan.ksplit > 1) {
+      float* slotbuf = a.slots + (static_cast<int64_t>(piece) * 32 + lane) * (8 * NT);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+          __stcg(reinterpret_cast<float4*>(slotbuf + (h * NT + j) * 4),
+                 make_float4(acc[h][j][0], acc[h][j][1], acc[h][j][2], acc[h][j][3]));
+      __threadfence();
+      __syncwarp();
+      int prior = 0;
+      if (lane == 0) prior = atomicAdd(&a.counters[rb], 1);
+      prior = __shfl_sync(0xffffffffu, prior, 0);
+      if (prior != plan.ksplit - 1) continue;
+      __threadfence();
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < NT; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0.f;
+      for (int p = 0; p < plan.ksplit; ++p) {
+        const float* src = a.slots + (static_cast<int64_t>(rb * plan.ksplit + p) * 32 + lane) * (8 * NT);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(src + (h * NT + j) * 4));
+            acc[h][j][0] += v.x;
+            acc[h][j][1] += v.y;
+            acc[h][j][2] += v.z;
+            acc[h][j][3] += v.w;
+          }
+      }
+      if (lane == 0) a.counters[rb] = 0;
+    }
+
+    // ---------------------------------------------------------------- epilogue
+    if constexpr (EPI == kGemvStore || EPI == kGemvResidual) {
+      bf16* out = static_cast<bf16*>(a.out);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int n = rb * 32 + h * 16 + g + 8 * (e >> 1);
+            const int b = 8 * j + 2 * t + (e & 1);
+            if (b >= B || n >= a.rows) continue;
+            bf16* dst = out + b * a.out_stride + n;
+            if constexpr (EPI == kGemvStore) *dst = __float2bfloat16_rn(acc[h][j][e]);
+            else *dst = __float2bfloat16_rn(ldcg_bf16(dst) + bf16_round(acc[h][j][e]));
+          }
+    } else if constexpr (EPI == kGemvSiluMul) {
+      bf16* out = static_cast<bf16*>(a.out);
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int col = rb * 16 + g + 8 * (e >> 1);
+          const int b = 8 * j + 2 * t + (e & 1);
+          if (b >= B) continue;
+          const float gate = bf16_round(acc[0][j][e]);
+          const float up = bf16_round(acc[1][j][e]);
+          const float act = bf16_round(gate / (1.0f + expf(-gate)));
+          out[b * a.out_stride + col] = __float2bfloat16_rn(act * up);
+        }
+    } else {  // fp32 logits + per-row-block sampling records
+      float* logits = static_cast<float*>(a.out);
+      const float temperature =
+          a.state ? __int_as_float(static_cast<int>(a.state[IPE_STATE_TEMPERATURE])) : a.temperature;
+      const uint64_t seed = a.state ? static_cast<uint64_t>(a.state[IPE_STATE_SEED]) : a.seed;
+      const int64_t step = a.state ? a.state[IPE_STATE_STEP] : 0;
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int b = 8 * j + 2 * t + c;
+          Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) {
+              const int n = rb * 32 + h * 16 + g + 8 * r;
+              if (b < B && n < a.rows) {
+                const float l = bf16_round(acc[h][j][2 * r + c]);
+                logits[b * a.out_stride + n] = l;
+                Stat y{l, 1.f, n, -INFINITY, 0x7fffffff};
+                if (temperature > 0.f) {
+                  y.gs = l / temperature - logf(-logf(uniform01(seed, n, b, step)));
+                  y.garg = n;
+                }
+                st = merge(st, y);
+              }
+            }
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
+                   __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
+                   __shfl_xor_sync(0xffffffffu, st.garg, o)};
+            st = merge(st, y);
+          }
+          if (g == 0 && b < B) {
+            float* rec = a.partials + (static_cast<int64_t>(rb) * B + b) * IPE_PARTIAL_WORDS;
+            rec[0] = st.m;
+            rec[1] = st.s;
+            rec[2] = st.gs;
+            rec[3] = 0.f;
+            rec[4] = __int_as_float(st.arg);
+            rec[5] = __int_as_float(st.garg);
+          }
+        }
     }
   }
 }
 
-template <int NT, int RT, bool NORM, int EPI, int U>
-cudaError_t launch_one(const GemvArgs& a, cudaStream_t stream) {
-  const size_t smem = gemv_smem_bytes(a);
-  auto kernel = gemv_kernel<NT, RT, NORM, EPI, U>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+Plan make_plan(const GemvArgs& a) {
+  Plan p{};
+  p.row_blocks = a.epilogue == kGemvSiluMul ? a.rows / 32 : (a.rows + 31) / 32;
+  const int units = a.k / kSubK;  // tiles per row block
+  const int sms = sm_count();
+  int split = 1;
+  if (a.epilogue != kGemvLogits) {
+    // Smallest power-of-two split that gives every SM >= 8 pieces and <= 5% imbalance.
+    for (int s = 1; s <= units; s *= 2) {
+      if (units % s) break;
+      split = s;
+      const int64_t pieces = static_cast<int64_t>(p.row_blocks) * s;
+      const double per = static_cast<double>(pieces) / sms;
+      const double balance = per / static_cast<double>((pieces + sms - 1) / sms);
+      if (pieces >= 8LL * sms && balance >= 0.95) break;
+    }
+  }
+  p.ksplit = split;
+  p.piece_k = a.k / split;
+  p.pieces = p.row_blocks * split;
+  p.tiles = static_cast<int64_t>(p.row_blocks) * units;
+  const size_t act = static_cast<size_t>(a.batch) * (a.k + kPad) * 2;
+  p.stages = kMaxStages;
+  p.act_smem = kFixedSmem + static_cast<size_t>(kMaxStages) * kTileBytes + act + 16 <= kSmemLimit;
+  p.smem = kFixedSmem + static_cast<size_t>(p.stages) * kTileBytes + (p.act_smem ? act + 16 : 0);
+  return p;
+}
+
+template <int NT, int EPI, bool NORM, bool ACT>
+cudaError_t launch_one(const GemvArgs& a, const Plan& plan, cudaStream_t stream) {
+  auto kernel = stream_gemv_kernel<NT, EPI, NORM, ACT>;
+  static bool configured = false;
+  if (!configured) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kSmemLimit + 1024));
     if (e != cudaSuccess) return e;
+    configured = true;
   }
-  const int per_block = EPI == kGemvSiluMul ? 16 : 16 * RT;
-  const int logical_rows = EPI == kGemvSiluMul ? a.rows / 2 : a.rows;
-  const unsigned blocks = static_cast<unsigned>((logical_rows + per_block - 1) / per_block);
-  kernel<<<blocks, kThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+  const int grid = plan.pieces < sm_count() ? plan.pieces : sm_count();
+  return launch_pdl(kernel, dim3(grid), dim3(kThreads), plan.smem, stream, a, plan);
 }
 
-template <int NT>
-cudaError_t dispatch(const GemvArgs& a, cudaStream_t stream) {
+template <int NT, bool ACT>
+cudaError_t dispatch(const GemvArgs& a, const Plan& plan, cudaStream_t stream) {
   switch (a.epilogue) {
-    case kGemvStore:
-      return launch_one<NT, 1, true, kGemvStore, 4>(a, stream);
-    case kGemvResidual:
-      return launch_one<NT, 1, false, kGemvResidual, 4>(a, stream);
-    case kGemvSiluMul:
-      return launch_one<NT, 2, true, kGemvSiluMul, 2>(a, stream);
-    default:
-      return launch_one<NT, 2, true, kGemvLogits, 2>(a, stream);
+    case kGemvStore: return launch_one<NT, kGemvStore, true, ACT>(a, plan, stream);
+    case kGemvResidual: return launch_one<NT, kGemvResidual, false, ACT>(a, plan, stream);
+    case kGemvSiluMul: return launch_one<NT, kGemvSiluMul, true, ACT>(a, plan, stream);
+    default: return launch_one<NT, kGemvLogits, true, ACT>(a, plan, stream);
   }
 }
 
-// -------------------------------------------------------------------------------- sampling
-struct Stat {
-  float m, s;
-  int arg;
-  float gs;
-  int garg;
-};
-
-__device__ __forceinline__ Stat merge(Stat x, const Stat& y) {
-  if (y.m > x.m) {
-    x.s = (x.m == -INFINITY ? 0.f : x.s * expf(x.m - y.m)) + y.s;
-    x.m = y.m;
-    x.arg = y.arg;
-  } else if (y.m > -INFINITY) {
-    x.s += y.s * expf(y.m - x.m);
-    if (y.m == x.m && y.arg < x.arg) x.arg = y.arg;
+// ------------------------------------------------------------------------------ tile builder
+// One thread per 16-byte chunk of the tiled output.
+__global__ void decode_tiles_kernel(const bf16* __restrict__ w, const bf16* __restrict__ w2, bf16* __restrict__ out,
+                                    int rows, int k, int64_t chunks) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= chunks) return;
+  // idx = ((((rb * ku_row + ku) * 2 + h) * 2 + j) * 16 + r) * 8 + pc
+  const int pc = static_cast<int>(idx & 7);
+  const int r = static_cast<int>((idx >> 3) & 15);
+  const int j = static_cast<int>((idx >> 7) & 1);
+  const int h = static_cast<int>((idx >> 8) & 1);
+  const int64_t tile = idx >> 9;
+  const int ku_row = k / kSubK;
+  const int ku = static_cast<int>(tile % ku_row);
+  const int64_t rb = tile / ku_row;
+  const int lc = pc ^ (r & 7);
+  const int col = ku * kSubK + j * 64 + lc * 8;
+  int64_t row;
+  const bf16* src;
+  if (w2) {  // gate / up pair: half 0 from w, half 1 from w2, rows 16 rb + r
+    row = rb * 16 + r;
+    src = h == 0 ? w : w2;
+  } else {
+    row = rb * 32 + h * 16 + r;
+    src = w;
   }
-  if (y.gs > x.gs || (y.gs == x.gs && y.garg < x.garg)) {
-    x.gs = y.gs;
-    x.garg = y.garg;
-  }
-  return x;
-}
-
-__global__ void __launch_bounds__(1024) sample_kernel(const float* __restrict__ partials, int parts,
-                                                      const float* __restrict__ logits, int B, int V,
-                                                      float temperature_arg, int64_t* state, int64_t* tokens,
-                                                      float* logprobs, int64_t stride, int64_t* next_tokens) {
-  __shared__ Stat shared[32];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int per_row = 32 / B;  // warps per batch row (B <= 16)
-  const int b = warp / per_row, sub = warp % per_row;
-  const int64_t step = state ? state[IPE_STATE_STEP] : 0;
-  const float temperature = state ? __int_as_float(static_cast<int>(state[IPE_STATE_TEMPERATURE])) : temperature_arg;
-  Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
-  if (b < B) {
-    for (int p = sub * 32 + lane; p < parts; p += per_row * 32) {
-      const float* rec = partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS;
-      st = merge(st, Stat{rec[0], rec[1], __float_as_int(rec[4]), rec[2], __float_as_int(rec[5])});
-    }
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
-           __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
-           __shfl_xor_sync(0xffffffffu, st.garg, o)};
-    st = merge(st, y);
-  }
-  if (lane == 0) shared[warp] = st;
-  __syncthreads();
-  if (threadIdx.x < B) {
-    const int row = threadIdx.x;
-    Stat r = shared[row * per_row];
-    for (int i = 1; i < per_row; ++i) r = merge(r, shared[row * per_row + i]);
-    const int token = temperature > 0.f ? r.garg : r.arg;
-    const float logit = logits[static_cast<int64_t>(row) * V + token];
-    const float lp = (logit - r.m) - logf(r.s);
-    tokens[row * stride + step] = token;
-    logprobs[row * stride + step] = lp;
-    if (next_tokens) next_tokens[row] = token;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0 && state) state[IPE_STATE_STEP] = step + 1;
-}
-
-// Token and untempered log-probability per row of a logits matrix [rows, V]: one CTA per row.
-// Gumbel noise for (seed, row, vocab id) when temperature > 0.
-__global__ void __launch_bounds__(256) sample_logits_kernel(const float* __restrict__ logits, int V, float temperature,
-                                                            uint64_t seed, int64_t* tokens, float* logprobs,
-                                                            int64_t stride) {
-  const int64_t row = blockIdx.x;
-  const float* l = logits + row * V;
-  Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
-  for (int v = threadIdx.x; v < V; v += blockDim.x) {
-    const float x = l[v];
-    Stat y{x, 1.f, v, -INFINITY, 0x7fffffff};
-    if (temperature > 0.f) {
-      const uint32_t r = philox_word(static_cast<uint32_t>(v), static_cast<uint32_t>(row),
-                                     static_cast<uint32_t>(row >> 32), 0xffffffffu, static_cast<uint32_t>(seed),
-                                     static_cast<uint32_t>(seed >> 32));
-      const float u = static_cast<float>(r >> 8) * (1.0f / 16777216.0f);
-      y.gs = x / temperature - logf(-logf(u));
-      y.garg = v;
-    }
-    st = merge(st, y);
-  }
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
-           __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
-           __shfl_xor_sync(0xffffffffu, st.garg, o)};
-    st = merge(st, y);
-  }
-  __shared__ Stat shared[8];
-  if ((threadIdx.x & 31) == 0) shared[threadIdx.x >> 5] = st;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    Stat r = shared[0];
-    for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i) r = merge(r, shared[i]);
-    const int token = temperature > 0.f ? r.garg : r.arg;
-    tokens[row * stride] = token;
-    logprobs[row * stride] = (l[token] - r.m) - logf(r.s);
-  }
+  uint4 v = make_uint4(0, 0, 0, 0);
+  if (row < rows) v = *reinterpret_cast<const uint4*>(src + row * k + col);
+  *reinterpret_cast<uint4*>(out + idx * 8) = v;
 }
 
 }  // namespace
 
-int gemv_rows_per_block(int epilogue) { return epilogue == kGemvStore || epilogue == kGemvResidual ? 16 : 32; }
-
-size_t gemv_smem_bytes(const GemvArgs& a) {
+size_t gemv_workspace_bytes(const GemvArgs& a) {
+  const Plan p = make_plan(a);
+  if (p.ksplit == 1) return 0;
   const int nt = a.batch <= 8 ? 1 : 2;
-  const int rt = (a.epilogue == kGemvStore || a.epilogue == kGemvResidual) ? 1 : 2;
-  const bool norm = a.epilogue != kGemvResidual;
-  const size_t out = static_cast<size_t>(rt) * 16 * nt * 8;
-  size_t bytes = (kWarps + 1) * out * sizeof(float);
-  if (norm) bytes += static_cast<size_t>(a.batch) * (a.k + kPadElems) * 2;
-  return bytes;
+  return kCounterBytes + static_cast<size_t>(p.pieces) * 32 * 8 * nt * sizeof(float);
 }
 
-cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream) {
-  return a.batch <= 8 ? dispatch<1>(a, stream) : dispatch<2>(a, stream);
+size_t decode_tiles_bytes(int rows, int k, bool pair) {
+  const int64_t blocks = pair ? (rows + 15) / 16 : (rows + 31) / 32;
+  return static_cast<size_t>(blocks) * (k / kSubK) * kTileBytes;
 }
 
-void launch_sample(const float* partials, int parts, const float* logits, int batch, int vocab, float temperature,
-                   int64_t* state, int64_t* tokens, float* logprobs, int64_t stride, int64_t* next_tokens,
-                   cudaStream_t stream) {
-  sample_kernel<<<1, 1024, 0, stream>>>(partials, parts, logits, batch, vocab, temperature, state, tokens, logprobs,
-                                        stride, next_tokens);
+cudaError_t launch_decode_tiles(const void* w, const void* w2, void* out, int rows, int k, cudaStream_t stream) {
+  const int64_t chunks = static_cast<int64_t>(decode_tiles_bytes(rows, k, w2 != nullptr) / 16);
+  const unsigned blocks = static_cast<unsigned>((chunks + 255) / 256);
+  decode_tiles_kernel<<<blocks, 256, 0, stream>>>(static_cast<const bf16*>(w), static_cast<const bf16*>(w2),
+                                                   static_cast<bf16*>(out), rows, k, chunks);
+  return cudaGetLastError();
 }
 
-}  // namespace ipe
-
-namespace ipe {
-void launch_sample_logits(const float* logits, int64_t rows, int vocab, float temperature, uint64_t seed,
-                          int64_t* tokens, float* logprobs, int64_t stride, cudaStream_t stream) {
-  sample_logits_kernel<<<static_cast<unsigned>(rows), 256, 0, stream>>>(logits, vocab, temperature, seed, tokens,
-                                                                        logprobs, stride);
+cudaError_t launch_gemv(GemvArgs a, void* workspace, cudaStream_t stream, const char** message) {
+  const Plan plan = make_plan(a);
+  if (plan.row_blocks > static_cast<int>(kCounterBytes / sizeof(int)) && plan.ksplit > 1) {
+    *message = "too many row blocks for the split-K counters";
+    return cudaErrorInvalidValue;
+  }
+  if (plan.ksplit > 1) {
+    a.counters = static_cast<int*>(workspace);
+    a.slots = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + kCounterBytes);
+  }
+  if (a.batch <= 8) return plan.act_smem ? dispatch<1, true>(a, plan, stream) : dispatch<1, false>(a, plan, stream);
+  return plan.act_smem ? dispatch<2, true>(a, plan, stream) : dispatch<2, false>(a, plan, stream);
 }
+
 }  // namespace ipe

@@ -23,24 +23,29 @@ enum GemvEpilogue : int { kGemvStore = 0, kGemvResidual = 1, kGemvSiluMul = 2, k
 struct GemvArgs {
   const void* x;           // bf16 activations, row b at x + b * x_stride
   int64_t x_stride;
-  const void* norm_weight;  // non-null: RMSNorm x rows first (width k)
+  const void* norm_weight;  // RMSNorm weight for the norm-fused epilogues (width k)
   float eps;
-  const void* w;  // bf16 [rows, k]
+  const void* w;  // decode tiles of the bf16 [rows, k] weight (ipe_decode_tiles)
   int rows;       // weight rows (for SiLU: 2 * intermediate, interleaved in groups of 64)
   int k;
   int batch;
   void* out;  // bf16 (store / residual in-out / silu) or fp32 logits
   int64_t out_stride;
-  float* partials;  // logits: sampling partial records
+  float* partials;  // logits: sampling partial records, one per 32 rows
   float temperature;
   uint64_t seed;
   const int64_t* state;
   int epilogue;
   int* err;
+  float* slots;    // split-K partial tiles (set by launch_gemv from the workspace)
+  int* counters;   // split-K arrival counters, zero between launches
 };
-cudaError_t launch_gemv(const GemvArgs& a, cudaStream_t stream);
-int gemv_rows_per_block(int epilogue);
-size_t gemv_smem_bytes(const GemvArgs& a);
+// Bytes of the decode tile layout of a [rows, k] matrix (pair: two [rows, k] gate/up matrices).
+size_t decode_tiles_bytes(int rows, int k, bool pair);
+cudaError_t launch_decode_tiles(const void* w, const void* w2, void* out, int rows, int k, cudaStream_t stream);
+// Workspace bytes launch_gemv needs for `a` (0 when K is not split); zero-filled before first use.
+size_t gemv_workspace_bytes(const GemvArgs& a);
+cudaError_t launch_gemv(GemvArgs a, void* workspace, cudaStream_t stream, const char** message);
 
 void launch_sample(const float* partials, int parts, const float* logits, int batch, int vocab, float temperature,
                    int64_t* state, int64_t* tokens, float* logprobs, int64_t stride, int64_t* next_tokens,
@@ -54,6 +59,11 @@ int decode_attention_chunk();
 cudaError_t launch_decode_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                     int kv_heads, int capacity, int length, const int64_t* state, float* workspace,
                                     cudaStream_t stream);
+size_t fused_decode_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity);
+cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, const void* k_norm, const void* cos_t,
+                                          const void* sin_t, const int64_t* state, int start, void* k_cache,
+                                          void* v_cache, void* out, int batch, int q_heads, int kv_heads, int capacity,
+                                          float eps, void* workspace, int* err, cudaStream_t stream);
 cudaError_t launch_prefill_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                      int kv_heads, int tokens, int capacity, cudaStream_t stream);
 

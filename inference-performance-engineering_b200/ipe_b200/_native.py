@@ -29,15 +29,21 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_embed": (c_int, [_P, c_int64, _P, c_int64, c_int, _P, _P]),
     "ipe_qk_norm_rope_append": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P, _P, _P, _P,
                                         c_int, c_float, _P]),
-    "ipe_rmsnorm_qkv": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P]),
-    "ipe_linear_residual": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P]),
-    "ipe_rmsnorm_gate_up_silu": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P]),
+    "ipe_decode_linear_workspace": (c_size_t, [c_int, c_int, c_int]),
+    "ipe_decode_tiles": (c_int, [_P, _P, _P, c_int, c_int, _P]),
+    "ipe_decode_tiles_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "ipe_rmsnorm_qkv": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P, c_size_t, _P]),
+    "ipe_linear_residual": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P, c_size_t, _P]),
+    "ipe_rmsnorm_gate_up_silu": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_float, _P, c_size_t, _P]),
     "ipe_lm_head": (c_int, [_P, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_float, c_float, c_uint64, _P, _P]),
     "ipe_lm_head_parts": (c_int, [c_int]),
     "ipe_sample": (c_int, [_P, _P, c_int, c_int, c_float, _P, _P, _P, c_int64, _P, _P]),
     "ipe_sample_logits": (c_int, [_P, c_int64, c_int, c_float, c_uint64, _P, _P, _P]),
     "ipe_decode_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P, c_size_t, _P]),
     "ipe_decode_attention_workspace": (c_size_t, [c_int, c_int, c_int]),
+    "ipe_decode_attention_qkv": (c_int, [_P, _P, _P, _P, _P, c_int, _P, _P, _P, _P, c_int, c_int, c_int, c_int,
+                                         c_float, _P, c_size_t, _P]),
+    "ipe_decode_attention_qkv_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ipe_decode_attention_static_scratch": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P]),
     "ipe_prefill_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
     "ipe_gemm": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P]),

@@ -186,7 +186,7 @@ class Engine:
         """How many library kernels one `generate(prompt, new_tokens)` launches, by phase."""
         layers = self.loaded.config.num_hidden_layers
         prefill = 1 + layers * 8 + 2  # embed; norm, qkv, rope/append, attention, o, norm, gate/up, down; head, state
-        decode = 1 + layers * 7 + 2  # embed; qkv, rope/append, 2 attention, o, gate/up, down; head, advance
+        decode = 1 + layers * 5 + 2  # embed; qkv, fused attention, o, gate/up, down; head, advance
         return {"prefill": prefill, "decode_step": decode, "sample": 1,
                 "generate": 4 + prefill + new_tokens + (new_tokens - 1) * decode}
 
@@ -230,7 +230,7 @@ class Engine:
             prefill_layer(m, index, buf, self._k[index], self._v[index], batch, length, self.capacity, cos, sin,
                           stream)
         last = buf.x.data_ptr() + (length - 1) * c.hidden_size * 2
-        nat.check(lib.ipe_lm_head(last, length * c.hidden_size, m.final_norm.data_ptr(), m.lm_head.data_ptr(),
+        nat.check(lib.ipe_lm_head(last, length * c.hidden_size, m.final_norm.data_ptr(), m.t_lm_head.data_ptr(),
                                   self._buf.logits.data_ptr(), self._buf.partials.data_ptr(), batch, c.hidden_size,
                                   c.vocab_size, c.rms_norm_eps, 0.0, 0, self._buf.state.data_ptr(), stream),
                   "ipe_lm_head")
@@ -245,7 +245,7 @@ class Engine:
         for index in range(c.num_hidden_layers):
             decoder_layer(m, index, buf, self._k[index], self._v[index], batch, self.capacity, self._cos, self._sin,
                           stream)
-        nat.check(lib.ipe_lm_head(buf.x.data_ptr(), c.hidden_size, m.final_norm.data_ptr(), m.lm_head.data_ptr(),
+        nat.check(lib.ipe_lm_head(buf.x.data_ptr(), c.hidden_size, m.final_norm.data_ptr(), m.t_lm_head.data_ptr(),
                                   buf.logits.data_ptr(), buf.partials.data_ptr(), batch, c.hidden_size, c.vocab_size,
                                   c.rms_norm_eps, 0.0, 0, buf.state.data_ptr(), stream), "ipe_lm_head")
         nat.check(lib.ipe_state_add(buf.state.data_ptr(), nat.STATE_POS, 1, stream), "ipe_state_add")

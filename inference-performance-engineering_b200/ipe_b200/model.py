@@ -33,8 +33,21 @@ def rotary_rows(positions: torch.Tensor, head_dim: int, theta: float) -> tuple[t
     return angle.cos().to(torch.bfloat16), angle.sin().to(torch.bfloat16)
 
 
+def decode_tiles(w: torch.Tensor, w_up: torch.Tensor | None = None) -> torch.Tensor:
+    """The decode-tile layout the weight-streaming kernels read (see include/ipe_b200.h), built on
+    the GPU by ipe_decode_tiles from a row-major [rows, in] matrix (or a gate/up pair)."""
+    lib = nat.load()
+    rows, k = w.shape
+    tiles = torch.empty(int(lib.ipe_decode_tiles_bytes(rows, k, 1 if w_up is not None else 0)), dtype=torch.uint8,
+                        device=w.device)
+    nat.check(lib.ipe_decode_tiles(w.data_ptr(), None if w_up is None else w_up.data_ptr(), tiles.data_ptr(), rows, k,
+                                   torch.cuda.current_stream(w.device).cuda_stream), "ipe_decode_tiles")
+    return tiles
+
+
 class PackedLayer:
-    __slots__ = ("in_norm", "post_norm", "q_norm", "k_norm", "w_qkv", "w_o", "w_gate_up", "w_down", "ptr")
+    __slots__ = ("in_norm", "post_norm", "q_norm", "k_norm", "w_qkv", "w_o", "w_gate_up", "w_down", "t_qkv", "t_o",
+                 "t_gate_up", "t_down", "ptr")
 
     def __init__(self, layer, config):
         self.in_norm = layer.input_layernorm.contiguous()
@@ -48,8 +61,14 @@ class PackedLayer:
         up = layer.up_proj.reshape(i // g, g, h)
         self.w_gate_up = torch.stack((gate, up), dim=1).reshape(2 * i, h).contiguous()
         self.w_down = layer.down_proj.contiguous()
+        # decode: the same weights in the tile layout the streaming kernels copy in contiguous 8 KB pieces
+        self.t_qkv = decode_tiles(self.w_qkv)
+        self.t_o = decode_tiles(self.w_o)
+        self.t_gate_up = decode_tiles(layer.gate_proj.contiguous(), layer.up_proj.contiguous())
+        self.t_down = decode_tiles(self.w_down)
         self.ptr = {name: getattr(self, name).data_ptr() for name in
-                    ("in_norm", "post_norm", "q_norm", "k_norm", "w_qkv", "w_o", "w_gate_up", "w_down")}
+                    ("in_norm", "post_norm", "q_norm", "k_norm", "w_qkv", "w_o", "w_gate_up", "w_down", "t_qkv",
+                     "t_o", "t_gate_up", "t_down")}
 
 
 class PackedModel:
@@ -64,6 +83,7 @@ class PackedModel:
         self.final_norm = w.norm.contiguous()
         with torch.no_grad():
             self.layers = [PackedLayer(layer, c) for layer in w.layers]
+            self.t_lm_head = decode_tiles(self.lm_head)
         self.q_rows = c.num_attention_heads * c.head_dim
         self.kv_rows = c.num_key_value_heads * c.head_dim
         self.qkv_rows = self.q_rows + 2 * self.kv_rows
@@ -168,15 +188,22 @@ class DecodeBuffers:
         c, dev, bf = model.config, model.device, torch.bfloat16
         self.x = torch.empty((batch, c.hidden_size), dtype=bf, device=dev)
         self.qkv = torch.empty((batch, model.qkv_rows), dtype=bf, device=dev)
-        self.q = torch.empty((batch, c.num_attention_heads, 1, c.head_dim), dtype=bf, device=dev)
         self.attn = torch.empty((batch, model.q_rows), dtype=bf, device=dev)
         self.act = torch.empty((batch, c.intermediate_size), dtype=bf, device=dev)
         self.logits = torch.empty((batch, c.vocab_size), dtype=torch.float32, device=dev)
         parts = int(nat.load().ipe_lm_head_parts(c.vocab_size))
         self.parts = parts
         self.partials = torch.empty((parts, batch, nat.PARTIAL_WORDS), dtype=torch.float32, device=dev)
-        ws = int(nat.load().ipe_decode_attention_workspace(batch, c.num_attention_heads, capacity))
-        self.workspace = torch.empty(ws, dtype=torch.uint8, device=dev)
+        ws = int(nat.load().ipe_decode_attention_qkv_workspace(batch, c.num_attention_heads, c.num_key_value_heads,
+                                                                capacity))
+        # split-KV partial records and arrival counters of the fused decode attention (kept zeroed by it)
+        self.workspace = torch.zeros(ws, dtype=torch.uint8, device=dev)
+        lib = nat.load()
+        linear = max(int(lib.ipe_decode_linear_workspace(batch, rows, k)) for rows, k in (
+            (model.qkv_rows, c.hidden_size), (c.hidden_size, model.q_rows), (2 * c.intermediate_size, c.hidden_size),
+            (c.hidden_size, c.intermediate_size)))
+        # split-K partial tiles and arrival counters of the decode linear layers (kept zeroed by them)
+        self.linear_workspace = torch.zeros(max(linear, 256), dtype=torch.uint8, device=dev)
         self.state = torch.zeros(nat.STATE_WORDS, dtype=torch.int64, device=dev)
         self.tokens = torch.zeros(batch, dtype=torch.int64, device=dev)
 
@@ -188,20 +215,18 @@ def decode_layer(model: PackedModel, index: int, buf: DecodeBuffers, k_layer: to
     lib = nat.load()
     c, p = model.config, model.layers[index].ptr
     x, eps, state = buf.x.data_ptr(), c.rms_norm_eps, buf.state.data_ptr()
-    nat.check(lib.ipe_rmsnorm_qkv(x, p["in_norm"], p["w_qkv"], buf.qkv.data_ptr(), batch, c.hidden_size,
-                                  model.qkv_rows, eps, stream), "ipe_rmsnorm_qkv")
-    nat.check(lib.ipe_qk_norm_rope_append(buf.qkv.data_ptr(), batch, 1, c.num_attention_heads, c.num_key_value_heads,
-                                          p["q_norm"], p["k_norm"], cos.data_ptr(), sin.data_ptr(), 0, state,
-                                          buf.q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), capacity, eps,
-                                          stream), "ipe_qk_norm_rope_append")
-    nat.check(lib.ipe_decode_attention(buf.q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), buf.attn.data_ptr(),
-                                       batch, c.num_attention_heads, c.num_key_value_heads, capacity, 0, state,
-                                       buf.workspace.data_ptr(), buf.workspace.numel(), stream),
-              "ipe_decode_attention")
-    nat.check(lib.ipe_linear_residual(buf.attn.data_ptr(), p["w_o"], x, batch, model.q_rows, c.hidden_size, stream),
-              "ipe_linear_residual o_proj")
-    nat.check(lib.ipe_rmsnorm_gate_up_silu(x, p["post_norm"], p["w_gate_up"], buf.act.data_ptr(), batch,
-                                           c.hidden_size, c.intermediate_size, eps, stream),
+    ws, wsn = buf.linear_workspace.data_ptr(), buf.linear_workspace.numel()
+    nat.check(lib.ipe_rmsnorm_qkv(x, p["in_norm"], p["t_qkv"], buf.qkv.data_ptr(), batch, c.hidden_size,
+                                  model.qkv_rows, eps, ws, wsn, stream), "ipe_rmsnorm_qkv")
+    nat.check(lib.ipe_decode_attention_qkv(buf.qkv.data_ptr(), p["q_norm"], p["k_norm"], cos.data_ptr(),
+                                           sin.data_ptr(), 0, state, k_layer.data_ptr(), v_layer.data_ptr(),
+                                           buf.attn.data_ptr(), batch, c.num_attention_heads, c.num_key_value_heads,
+                                           capacity, eps, buf.workspace.data_ptr(), buf.workspace.numel(), stream),
+              "ipe_decode_attention_qkv")
+    nat.check(lib.ipe_linear_residual(buf.attn.data_ptr(), p["t_o"], x, batch, model.q_rows, c.hidden_size, ws, wsn,
+                                      stream), "ipe_linear_residual o_proj")
+    nat.check(lib.ipe_rmsnorm_gate_up_silu(x, p["post_norm"], p["t_gate_up"], buf.act.data_ptr(), batch,
+                                           c.hidden_size, c.intermediate_size, eps, ws, wsn, stream),
               "ipe_rmsnorm_gate_up_silu")
-    nat.check(lib.ipe_linear_residual(buf.act.data_ptr(), p["w_down"], x, batch, c.intermediate_size, c.hidden_size,
-                                      stream), "ipe_linear_residual down_proj")
+    nat.check(lib.ipe_linear_residual(buf.act.data_ptr(), p["t_down"], x, batch, c.intermediate_size, c.hidden_size,
+                                      ws, wsn, stream), "ipe_linear_residual down_proj")

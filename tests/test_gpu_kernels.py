@@ -33,6 +33,19 @@ def no_device_error():
     assert nat.device_error(reset=True) == 0
 
 
+def tiles(w, w_up=None):
+    """Decode tiles of a weight (or a gate/up pair) through the C-ABI tile builder."""
+    from ipe_b200.model import decode_tiles
+
+    return decode_tiles(w.contiguous(), None if w_up is None else w_up.contiguous())
+
+
+def linear_workspace(batch, rows, k):
+    """A zero-filled split-K workspace for the decode linear kernels (they keep it zeroed)."""
+    n = int(nat.load().ipe_decode_linear_workspace(batch, rows, k))
+    return torch.zeros(max(n, 16), dtype=torch.uint8, device=DEV)
+
+
 # ----------------------------------------------------------------------------------- rms_norm
 
 def contract_inputs(width, dtype, seed=0):
@@ -146,11 +159,47 @@ def test_rmsnorm_qkv_matches_fp32(batch, hidden, rows):
     x, w = rand((batch, hidden), 11), (1 + 0.1 * rand((hidden,), 12, dtype=torch.float32)).bfloat16()
     wq = rand((rows, hidden), 13, 0.02)
     out = torch.empty((batch, rows), dtype=torch.bfloat16, device=DEV)
-    nat.call("ipe_rmsnorm_qkv", x.data_ptr(), w.data_ptr(), wq.data_ptr(), out.data_ptr(), batch, hidden, rows,
-             1e-6, stream())
+    ws = linear_workspace(batch, rows, hidden)
+    tq = tiles(wq)
+    for _ in range(2):  # the second call reuses the workspace its first call left zeroed
+        nat.call("ipe_rmsnorm_qkv", x.data_ptr(), w.data_ptr(), tq.data_ptr(), out.data_ptr(), batch, hidden, rows,
+                 1e-6, ws.data_ptr(), ws.numel(), stream())
+    assert int(ws[: 4 * ((rows + 31) // 32)].count_nonzero()) == 0  # arrival counters back at zero
     ref = rmsnorm_ref(x, w, 1e-6).float() @ wq.float().T
     assert bf16_close(out, ref, rel=2 * BF16_REL, abs_=1e-3)[0] == 0
     no_device_error()
+
+
+def test_decode_linear_layers_can_share_one_workspace():
+    """Qwen3-1.7B shapes, one workspace for all four decode linear layers in turn, twice: every
+    call must match the same call on a fresh workspace bit for bit."""
+    batch, hidden, inter = 2, 2048, 6144
+    x = rand((batch, hidden), 50)
+    nw = (1 + 0.1 * rand((hidden,), 51, dtype=torch.float32)).bfloat16()
+    wq, wo = tiles(rand((4096, hidden), 52, 0.02)), tiles(rand((hidden, 2048), 53, 0.02))
+    wgu = tiles(rand((inter, hidden), 54, 0.02), rand((inter, hidden), 55, 0.02))
+    wd = tiles(rand((hidden, inter), 56, 0.02))
+    need = max(int(nat.load().ipe_decode_linear_workspace(batch, r, k))
+               for r, k in ((4096, hidden), (hidden, 2048), (2 * inter, hidden), (hidden, inter)))
+    shared = torch.zeros(need, dtype=torch.uint8, device=DEV)
+
+    def run(ws):
+        qkv = torch.empty((batch, 4096), dtype=torch.bfloat16, device=DEV)
+        act = torch.empty((batch, inter), dtype=torch.bfloat16, device=DEV)
+        y = x.clone()
+        p = (ws.data_ptr(), ws.numel(), stream())
+        nat.call("ipe_rmsnorm_qkv", y.data_ptr(), nw.data_ptr(), wq.data_ptr(), qkv.data_ptr(), batch, hidden, 4096,
+                 1e-6, *p)
+        nat.call("ipe_linear_residual", qkv.data_ptr(), wo.data_ptr(), y.data_ptr(), batch, 2048, hidden, *p)
+        nat.call("ipe_rmsnorm_gate_up_silu", y.data_ptr(), nw.data_ptr(), wgu.data_ptr(), act.data_ptr(), batch, hidden,
+                 inter, 1e-6, *p)
+        nat.call("ipe_linear_residual", act.data_ptr(), wd.data_ptr(), y.data_ptr(), batch, inter, hidden, *p)
+        return qkv, act, y
+
+    fresh = [run(torch.zeros(need, dtype=torch.uint8, device=DEV)) for _ in range(1)][0]
+    for _ in range(2):
+        for a, b in zip(run(shared), fresh):
+            assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize("batch", (1, 4, 16))
@@ -158,7 +207,10 @@ def test_rmsnorm_qkv_matches_fp32(batch, hidden, rows):
 def test_linear_residual_matches_fp32(batch, k, n):
     a, w, x = rand((batch, k), 14), rand((n, k), 15, 1 / k ** 0.5), rand((batch, n), 16)
     out = x.clone()
-    nat.call("ipe_linear_residual", a.data_ptr(), w.data_ptr(), out.data_ptr(), batch, k, n, stream())
+    ws = linear_workspace(batch, n, k)
+    tw = tiles(w)
+    nat.call("ipe_linear_residual", a.data_ptr(), tw.data_ptr(), out.data_ptr(), batch, k, n, ws.data_ptr(), ws.numel(),
+             stream())
     acc = a.float() @ w.float().T
     ref = x.float() + acc.bfloat16().float()
     bound = 2 * BF16_REL * (acc.abs() + x.float().abs()) + 1e-3
@@ -174,22 +226,24 @@ def test_rmsnorm_gate_up_silu_matches_fp32(batch, hidden, inter):
     packed = torch.stack((gate.view(inter // g, g, hidden), up.view(inter // g, g, hidden)), 1)
     packed = packed.reshape(2 * inter, hidden).contiguous()
     out = torch.empty((batch, inter), dtype=torch.bfloat16, device=DEV)
-    nat.call("ipe_rmsnorm_gate_up_silu", x.data_ptr(), w.data_ptr(), packed.data_ptr(), out.data_ptr(), batch, hidden,
-             inter, 1e-6, stream())
+    ws = linear_workspace(batch, 2 * inter, hidden)
+    tgu = tiles(gate, up)
+    nat.call("ipe_rmsnorm_gate_up_silu", x.data_ptr(), w.data_ptr(), tgu.data_ptr(), out.data_ptr(), batch, hidden,
+             inter, 1e-6, ws.data_ptr(), ws.numel(), stream())
     h = rmsnorm_ref(x, w, 1e-6).float()
     ref = (F.silu((h @ gate.float().T).bfloat16()) * (h @ up.float().T).bfloat16()).float()
     assert bf16_close(out, ref, rel=3 * BF16_REL, abs_=2e-3)[0] == 0
 
 
 @pytest.mark.parametrize("batch", (1, 2, 16))
-@pytest.mark.parametrize(("hidden", "vocab"), [(2048, 151936), (256, 2048), (128, 1000)])
+@pytest.mark.parametrize(("hidden", "vocab"), [(2048, 151936), (256, 2048), (128, 1024)])
 def test_lm_head_logits_and_greedy_sample(batch, hidden, vocab):
     x, w = rand((batch, hidden), 21), (1 + 0.1 * rand((hidden,), 22, dtype=torch.float32)).bfloat16()
     emb = rand((vocab, hidden), 23, 0.02)
     parts = ops.lm_head_parts(vocab)
     logits = torch.empty((batch, vocab), dtype=torch.float32, device=DEV)
     partials = torch.empty((parts, batch, nat.PARTIAL_WORDS), dtype=torch.float32, device=DEV)
-    nat.call("ipe_lm_head", x.data_ptr(), hidden, w.data_ptr(), emb.data_ptr(), logits.data_ptr(),
+    nat.call("ipe_lm_head", x.data_ptr(), hidden, w.data_ptr(), tiles(emb).data_ptr(), logits.data_ptr(),
              partials.data_ptr(), batch, hidden, vocab, 1e-6, 0.0, 0, None, stream())
     ref = rmsnorm_ref(x, w, 1e-6).float() @ emb.float().T
     assert torch.equal(logits, logits.bfloat16().float())
@@ -276,6 +330,44 @@ def test_decode_attention_reads_its_length_from_the_device_state():
              state.data_ptr(), ws.data_ptr(), ws.numel(), stream())
     ref = attention_ref(q, k[:, :, :pos + 1], v[:, :, :pos + 1], False).reshape(batch, hq * 128)
     assert bf16_close(out, ref, rel=2 * BF16_REL, abs_=2e-3)[0] == 0
+
+
+@pytest.mark.parametrize(("batch", "hq", "hkv", "pos", "cap"),
+                         [(1, 16, 8, 0, 64), (1, 16, 8, 31, 64), (2, 16, 8, 32, 64), (3, 16, 8, 700, 1024),
+                          (1, 16, 4, 99, 128), (2, 8, 8, 4099, 4352), (1, 32, 4, 40, 64)])
+def test_fused_decode_attention_matches_the_unfused_ops(batch, hq, hkv, pos, cap):
+    """q/k norm + RoPE + append + attention from the QKV output, against the oracle operators and
+    an fp32 attention; run twice so the second call sees the counters the first left at zero."""
+    eps = 1e-6
+    qkv = rand((batch, (hq + 2 * hkv) * 128), 40)
+    qn = (1 + 0.1 * rand((128,), 41, dtype=torch.float32)).bfloat16()
+    kn = (1 + 0.1 * rand((128,), 42, dtype=torch.float32)).bfloat16()
+    cos, sin = oq.rotary_tables(torch.arange(cap), 128, 1e6, torch.bfloat16)
+    cos, sin = cos.to(DEV), sin.to(DEV)
+    k = torch.full((batch, hkv, cap, 128), float("nan"), dtype=torch.bfloat16, device=DEV)
+    v = k.clone()
+    k[:, :, :pos] = rand((batch, hkv, pos, 128), 43) if pos else k[:, :, :0]
+    v[:, :, :pos] = rand((batch, hkv, pos, 128), 44) if pos else v[:, :, :0]
+    ws = torch.zeros(int(nat.load().ipe_decode_attention_qkv_workspace(batch, hq, hkv, cap)), dtype=torch.uint8,
+                     device=DEV)
+    outs = []
+    for _ in range(2):
+        out = torch.empty((batch, hq * 128), dtype=torch.bfloat16, device=DEV)
+        nat.call("ipe_decode_attention_qkv", qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
+                 sin.data_ptr(), pos, None, k.data_ptr(), v.data_ptr(), out.data_ptr(), batch, hq, hkv, cap, eps,
+                 ws.data_ptr(), ws.numel(), stream())
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    split = qkv.view(batch, 1, hq + 2 * hkv, 128)
+    rows = slice(pos, pos + 1)
+    q_ref = oq.apply_rotary(oq.qk_norm(split[:, :, :hq], qn, eps).transpose(1, 2), cos[rows], sin[rows])
+    k_ref = oq.apply_rotary(oq.qk_norm(split[:, :, hq:hq + hkv], kn, eps).transpose(1, 2), cos[rows], sin[rows])
+    assert bf16_close(k[:, :, rows], k_ref, rel=BF16_REL, abs_=1e-6)[0] == 0
+    assert torch.equal(v[:, :, rows], split[:, :, hq + hkv:].transpose(1, 2))
+    ref = attention_ref(q_ref, k[:, :, :pos + 1], v[:, :, :pos + 1], False).reshape(batch, hq * 128)
+    assert bf16_close(outs[0], ref, rel=2 * BF16_REL, abs_=2e-3)[0] == 0
+    counters = ws[: 4 * batch * hkv].view(torch.int32)
+    assert int(counters.count_nonzero()) == 0
 
 
 @pytest.mark.parametrize(("batch", "hq", "hkv", "tokens", "cap"),

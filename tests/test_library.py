@@ -45,9 +45,11 @@ def test_the_binding_declares_nothing_the_header_lacks():
     ("ipe_gemm", (16, 16, 16, 128, 128, 48, 0, None, None)),
     ("ipe_gemm", (16, 16, 16, 128, 128, 64, 1, None, None)),
     ("ipe_gemm", (16, 16, 16, 128, 128, 64, 9, None, None)),
-    ("ipe_rmsnorm_qkv", (16, 16, 16, 16, 17, 2048, 4096, 1e-6, None)),
-    ("ipe_rmsnorm_qkv", (16, 16, 16, 16, 1, 2047, 4096, 1e-6, None)),
-    ("ipe_rmsnorm_gate_up_silu", (16, 16, 16, 16, 1, 2048, 100, 1e-6, None)),
+    ("ipe_rmsnorm_qkv", (16, 16, 16, 16, 17, 2048, 4096, 1e-6, 16, 1 << 30, None)),
+    ("ipe_rmsnorm_qkv", (16, 16, 16, 16, 1, 2047, 4096, 1e-6, 16, 1 << 30, None)),
+    ("ipe_rmsnorm_qkv", (16, 16, 16, 16, 1, 2048, 4096, 1e-6, None, 0, None)),
+    ("ipe_linear_residual", (16, 16, 16, 1, 2048, 2048, 16, 16, None)),
+    ("ipe_rmsnorm_gate_up_silu", (16, 16, 16, 16, 1, 2048, 100, 1e-6, 16, 1 << 30, None)),
     ("ipe_decode_attention", (16, 16, 16, 16, 1, 16, 8, 64, 65, None, 16, 1 << 20, None)),
     ("ipe_decode_attention", (16, 16, 16, 16, 1, 12, 8, 64, 8, None, 16, 1 << 20, None)),
     ("ipe_decode_attention", (16, 16, 16, 16, 1, 16, 8, 64, 8, None, 16, 0, None)),
