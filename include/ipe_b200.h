@@ -213,6 +213,57 @@ int ipe_prefill_attention(const void* q, const void* k_cache, const void* v_cach
 int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epilogue,
              const void* residual, void* stream);
 
+/* ------------------------------------------------------------------ whole decode step */
+
+/* One decoder layer's operands for ipe_decode_step (device pointers). */
+typedef struct {
+  const void* input_layernorm;          /* bf16 [hidden]                                    */
+  const void* post_attention_layernorm; /* bf16 [hidden]                                    */
+  const void* q_norm;                   /* bf16 [128]                                       */
+  const void* k_norm;                   /* bf16 [128]                                       */
+  const void* qkv_tiles;                /* decode tiles of q_proj | k_proj | v_proj          */
+  const void* o_tiles;                  /* decode tiles of o_proj                            */
+  const void* gate_up_tiles;            /* decode tiles of the (gate_proj, up_proj) pair     */
+  const void* down_tiles;               /* decode tiles of down_proj                         */
+  void* k_cache;                        /* bf16 [batch_rows, kv_heads, capacity, 128]        */
+  void* v_cache;
+} ipe_layer_desc;
+
+/* Everything one decode step reads and writes. Device pointers unless stated. */
+typedef struct {
+  int layers, hidden, intermediate, q_heads, kv_heads, vocab, capacity, batch;
+  float eps;
+  const ipe_layer_desc* layer_descs; /* device array of `layers` descriptors                 */
+  const void* embed;                 /* bf16 [vocab, hidden], row-major (the input embedding) */
+  const void* lm_head_tiles;         /* decode tiles of the (tied) LM head                    */
+  const void* final_norm;            /* bf16 [hidden]                                         */
+  const void* cos_table;             /* bf16 [capacity, 128]                                  */
+  const void* sin_table;
+  int64_t* state;                    /* int64[IPE_STATE_WORDS]: position read, then advanced */
+  int64_t* tokens;                   /* [batch] input IDs; the sampled IDs when sampling      */
+  void* x;                           /* bf16 [batch, hidden] residual stream                  */
+  void* qkv;                         /* bf16 [batch, (q_heads + 2 kv_heads) * 128]            */
+  void* attn;                        /* bf16 [batch, q_heads * 128]                           */
+  void* act;                         /* bf16 [batch, intermediate]                            */
+  float* logits;                     /* fp32 [batch, vocab]                                   */
+  float* partials;                   /* [ipe_lm_head_parts(vocab)][batch][IPE_PARTIAL_WORDS]  */
+  void* workspace;                   /* ipe_decode_step_workspace bytes, zero-filled once     */
+  size_t workspace_bytes;
+  int64_t* history_tokens;           /* nullable: sample the next token into [b*stride+step] */
+  float* history_logprobs;
+  int64_t history_stride;
+} ipe_decode_step_desc;
+
+/* One whole decode step (embedding, all layers, final norm, LM head, and the sampler when
+ * history_tokens is set) as ONE persistent cooperative kernel, one CTA per SM: a producer warp
+ * per SM streams every phase's decode tiles back to back with bulk copies, consumer warps meet at
+ * bounded-spin grid barriers between phases. Reads the position from state[IPE_STATE_POS] and
+ * advances it (and state[IPE_STATE_STEP] when sampling) at the end. Deterministic. Replaces
+ * src/ipe/engine.py:84-111 (decode -> _step) and, with sampling, one iteration of
+ * src/ipe/engine.py:137-147. */
+int ipe_decode_step(const ipe_decode_step_desc* desc, void* stream);
+size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capacity);
+
 /* ------------------------------------------------------------------ step state */
 
 int ipe_state_set(int64_t* state, int index, int64_t value, void* stream);

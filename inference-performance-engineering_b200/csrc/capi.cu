@@ -326,6 +326,36 @@ int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epi
   return cuda_status(e, "ipe_gemm");
 }
 
+size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capacity) {
+  if (batch < 1 || q_heads < 1 || kv_heads < 1 || capacity < 1) return 0;
+  return ipe::decode_step_workspace_bytes(batch, q_heads, kv_heads, capacity);
+}
+
+int ipe_decode_step(const ipe_decode_step_desc* d, void* stream) {
+  if (!d) return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: null descriptor");
+  if (!d->layer_descs || !d->embed || !d->lm_head_tiles || !d->final_norm || !d->cos_table || !d->sin_table ||
+      !d->state || !d->tokens || !d->x || !d->qkv || !d->attn || !d->act || !d->logits || !d->partials ||
+      !d->workspace)
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: null pointer in the descriptor");
+  if (d->layers < 1 || d->batch < 1 || d->batch > 16 || d->capacity < 1 || d->vocab < 1 || d->q_heads < 1 ||
+      d->kv_heads < 1 || d->q_heads % d->kv_heads)
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: bad sizes");
+  const int group = d->q_heads / d->kv_heads;
+  if (group != 1 && group != 2 && group != 4 && group != 8)
+    return fail(IPE_ERR_UNSUPPORTED, "ipe_decode_step: %d query heads per KV head", group);
+  if (d->hidden % 128 || d->intermediate % 128 || d->vocab % 32)
+    return fail(IPE_ERR_UNSUPPORTED, "ipe_decode_step: hidden / intermediate must be multiples of 128, vocab of 32");
+  if (d->history_tokens && (!d->history_logprobs || d->history_stride < 1))
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: history needs logprobs and a stride");
+  if (d->workspace_bytes < ipe_decode_step_workspace(d->batch, d->q_heads, d->kv_heads, d->capacity))
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: workspace of %zu bytes needed",
+                ipe_decode_step_workspace(d->batch, d->q_heads, d->kv_heads, d->capacity));
+  const char* message = nullptr;
+  cudaError_t e = ipe::launch_decode_step(*d, device_error_word(), as_stream(stream), &message);
+  if (e != cudaSuccess && message) return fail(IPE_ERR_CUDA, "ipe_decode_step: %s", message);
+  return cuda_status(e, "ipe_decode_step");
+}
+
 int ipe_state_set(int64_t* state, int index, int64_t value, void* stream) {
   if (!state || index < 0 || index >= IPE_STATE_WORDS) return fail(IPE_ERR_ARGUMENT, "ipe_state_set: bad arguments");
   ipe::launch_state_update(state, index, value, false, as_stream(stream));

@@ -25,6 +25,7 @@
 #include "common.cuh"
 #include "launch.h"
 #include "sampling.cuh"
+#include "stream_tile.cuh"
 #include "tensor_map.h"
 
 namespace ipe {
@@ -33,39 +34,12 @@ namespace {
 constexpr int kConsumers = 4;
 constexpr int kSlotsPerWarp = 3;
 constexpr int kThreads = 32 * (kConsumers + 1);
-constexpr int kTileBytes = 8192;  // 32 rows x 128 bf16
-constexpr int kBoxBytes = 2048;   // 16 rows x 64 bf16
-constexpr int kSubK = 128;
+constexpr int kSubK = kTileK;
 constexpr int kMaxStages = kConsumers * kSlotsPerWarp;
 constexpr int kPad = 32;  // bf16 elements of padding per staged activation row
 constexpr size_t kCounterBytes = 32768;  // arrival counters for up to 8192 row blocks
 constexpr size_t kSmemLimit = 200 * 1024;
 constexpr size_t kFixedSmem = 1024 + 2 * kMaxStages * 8 + 16 * 4 + 64;
-
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-__device__ __forceinline__ uint4 lds128(uint32_t addr) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
-  return v;
-}
-
-__device__ __forceinline__ void named_barrier(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(smem_addr(bar))
-               : "memory");
-}
 
 struct Plan {
   int row_blocks;
@@ -233,28 +207,7 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const GemvArgs
         ok = false;
         break;
       }
-      const uint32_t base = smem_addr(ring + slot * kTileBytes);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        // 32-column chunk c lives in box (h, c / 2); its 16-byte piece t is logical chunk
-        // (c % 2) * 4 + t of the 128-byte row, stored at that index XOR (row % 8).
-        const int chunk = (c & 1) * 4 + t;
-        uint4 w[2][2];
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int r = 0; r < 2; ++r) {
-            const int row = g + 8 * r;
-            w[h][r] = lds128(base + (h * 2 + (c >> 1)) * kBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
-          }
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-#pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            mma16816(acc[h][j], w[h][0].x, w[h][1].x, w[h][0].y, w[h][1].y, xv[c][j].x, xv[c][j].y);
-            mma16816(acc[h][j], w[h][0].z, w[h][1].z, w[h][0].w, w[h][1].w, xv[c][j].z, xv[c][j].w);
-          }
-      }
+      consume_tile<NT>(acc, smem_addr(ring + slot * kTileBytes), xv, g, t);
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[slot]);
     }
@@ -297,81 +250,8 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const GemvArgs
     }
 
     // ---------------------------------------------------------------- epilogue
-    if constexpr (EPI == kGemvStore || EPI == kGemvResidual) {
-      bf16* out = static_cast<bf16*>(a.out);
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int j = 0; j < NT; ++j)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int n = rb * 32 + h * 16 + g + 8 * (e >> 1);
-            const int b = 8 * j + 2 * t + (e & 1);
-            if (b >= B || n >= a.rows) continue;
-            bf16* dst = out + b * a.out_stride + n;
-            if constexpr (EPI == kGemvStore) *dst = __float2bfloat16_rn(acc[h][j][e]);
-            else *dst = __float2bfloat16_rn(ldcg_bf16(dst) + bf16_round(acc[h][j][e]));
-          }
-    } else if constexpr (EPI == kGemvSiluMul) {
-      bf16* out = static_cast<bf16*>(a.out);
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int col = rb * 16 + g + 8 * (e >> 1);
-          const int b = 8 * j + 2 * t + (e & 1);
-          if (b >= B) continue;
-          const float gate = bf16_round(acc[0][j][e]);
-          const float up = bf16_round(acc[1][j][e]);
-          const float act = bf16_round(gate / (1.0f + expf(-gate)));
-          out[b * a.out_stride + col] = __float2bfloat16_rn(act * up);
-        }
-    } else {  // fp32 logits + per-row-block sampling records
-      float* logits = static_cast<float*>(a.out);
-      const float temperature =
-          a.state ? __int_as_float(static_cast<int>(a.state[IPE_STATE_TEMPERATURE])) : a.temperature;
-      const uint64_t seed = a.state ? static_cast<uint64_t>(a.state[IPE_STATE_SEED]) : a.seed;
-      const int64_t step = a.state ? a.state[IPE_STATE_STEP] : 0;
-#pragma unroll
-      for (int j = 0; j < NT; ++j)
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          const int b = 8 * j + 2 * t + c;
-          Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int r = 0; r < 2; ++r) {
-              const int n = rb * 32 + h * 16 + g + 8 * r;
-              if (b < B && n < a.rows) {
-                const float l = bf16_round(acc[h][j][2 * r + c]);
-                logits[b * a.out_stride + n] = l;
-                Stat y{l, 1.f, n, -INFINITY, 0x7fffffff};
-                if (temperature > 0.f) {
-                  y.gs = l / temperature - logf(-logf(uniform01(seed, n, b, step)));
-                  y.garg = n;
-                }
-                st = merge(st, y);
-              }
-            }
-#pragma unroll
-          for (int o = 4; o < 32; o <<= 1) {
-            Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
-                   __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
-                   __shfl_xor_sync(0xffffffffu, st.garg, o)};
-            st = merge(st, y);
-          }
-          if (g == 0 && b < B) {
-            float* rec = a.partials + (static_cast<int64_t>(rb) * B + b) * IPE_PARTIAL_WORDS;
-            rec[0] = st.m;
-            rec[1] = st.s;
-            rec[2] = st.gs;
-            rec[3] = 0.f;
-            rec[4] = __int_as_float(st.arg);
-            rec[5] = __int_as_float(st.garg);
-          }
-        }
-    }
+    EpilogueArgs ea{a.out, a.out_stride, a.rows, B, a.partials, a.state, a.temperature, a.seed};
+    row_block_epilogue<EPI, NT>(acc, rb, lane, ea);
   }
 }
 

@@ -6,6 +6,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "ipe_b200.h"
+
 namespace ipe {
 
 void launch_rmsnorm(const void* x, const void* w, void* out, int64_t rows, int width, float eps, bool bf16_io,
@@ -66,6 +68,10 @@ cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, c
                                           float eps, void* workspace, int* err, cudaStream_t stream);
 cudaError_t launch_prefill_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                      int kv_heads, int tokens, int capacity, cudaStream_t stream);
+
+// Whole decode step (decode_step.cu).
+size_t decode_step_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity);
+cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStream_t stream, const char** message);
 
 // tcgen05 GEMM (gemm_tcgen05.cu). Returns a CUDA error or cudaSuccess; *message set on failure.
 cudaError_t launch_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epilogue,

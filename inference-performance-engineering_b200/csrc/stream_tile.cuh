@@ -1,0 +1,245 @@
+// Device pieces shared by the weight-streaming kernels (per-op GEMV and the decode-step kernel):
+// the decode-tile format, bulk copies into shared memory, the tensor-core consumption of one tile,
+// and the linear-layer epilogues with the reference's rounding points.
+//
+// Decode tile: 32 output rows (for SiLU*up: 16 gate rows, then the 16 matching up rows) x 128
+// reduction columns = 8 KB, laid out [half (2)][64-column box (2)][row (16)][128 bytes] with the
+// 16-byte chunks of each 128-byte row segment XOR-swizzled by (row % 8), so that the 16-byte
+// shared-memory reads of a warp are conflict-free. Tiles of one row block are adjacent.
+#pragma once
+
+#include "common.cuh"
+#include "launch.h"
+#include "sampling.cuh"
+
+namespace ipe {
+
+constexpr int kTileBytes = 8192;  // 32 rows x 128 bf16
+constexpr int kTileBoxBytes = 2048;  // 16 rows x 64 bf16
+constexpr int kTileK = 128;
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint4 lds128(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
+  return v;
+}
+
+__device__ __forceinline__ void named_barrier(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+
+// acc[h][j] += tile rows (h, g / g+8) x activations xv[c][j] (batch columns 8j..8j+7) over the
+// tile's 128 columns. The MMA's K order is permuted identically for A (weights, 16-byte chunk of
+// 8 consecutive columns per thread) and B (activations, the same 8 columns), so the dot products
+// are unchanged while every read is one contiguous 16 bytes.
+template <int NT>
+__device__ __forceinline__ void consume_tile(float (&acc)[2][NT][4], uint32_t base, const uint4 (&xv)[4][NT], int g,
+                                             int t) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int chunk = (c & 1) * 4 + t;
+    uint4 w[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int row = g + 8 * r;
+        w[h][r] = lds128(base + (h * 2 + (c >> 1)) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        mma16816(acc[h][j], w[h][0].x, w[h][1].x, w[h][0].y, w[h][1].y, xv[c][j].x, xv[c][j].y);
+        mma16816(acc[h][j], w[h][0].z, w[h][1].z, w[h][0].w, w[h][1].w, xv[c][j].z, xv[c][j].w);
+      }
+  }
+}
+
+// Stage B activation rows (row b at src + b * src_stride, K wide) in shared memory xs (row stride
+// xs_stride), RMS-normalised with weight norm_w when it is non-null: bf16(w * bf16(x * rstd)), the
+// reference's two roundings. rstd[b] receives the scale. The nwarps calling warps issue 8
+// independent 16-byte loads per lane before using any, so a row costs one L2 round trip (two when
+// K > 2048 and the row is normalised). to_smem = false computes rstd only. Callers synchronise.
+__device__ __forceinline__ void stage_rows(const bf16* src, int64_t src_stride, const bf16* norm_w, float eps, int B,
+                                           int K, bf16* xs, int xs_stride, float* rstd, int warp_id, int nwarps,
+                                           int lane, bool to_smem) {
+  const int chunks = K / 8;
+  if (norm_w) {
+    for (int b = warp_id; b < B; b += nwarps) {
+      const bf16* xr = src + b * src_stride;
+      uint4 v[8];
+      float ss = 0.f;
+      for (int base = 0; base < chunks; base += 256) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c = base + u * 32 + lane;
+          v[u] = c < chunks ? ldcg16(xr + c * 8) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          float f[8];
+          unpack8(v[u], f);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+        }
+      }
+      ss = warp_sum(ss);
+      const float r = rsqrtf(ss / static_cast<float>(K) + eps);
+      if (lane == 0) rstd[b] = r;
+      if (!to_smem) continue;
+      for (int base = 0; base < chunks; base += 256) {
+        if (chunks > 256) {  // the row did not fit one round: load this round again
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int c = base + u * 32 + lane;
+            v[u] = c < chunks ? ldcg16(xr + c * 8) : make_uint4(0, 0, 0, 0);
+          }
+        }
+        uint4 wv[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c = base + u * 32 + lane;
+          wv[u] = c < chunks ? ldg16(norm_w + c * 8) : make_uint4(0, 0, 0, 0);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int c = base + u * 32 + lane;
+          if (c >= chunks) continue;
+          float f[8], wf[8];
+          unpack8(v[u], f);
+          unpack8(wv[u], wf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * r);
+          *reinterpret_cast<uint4*>(xs + b * xs_stride + c * 8) = pack8(f);
+        }
+      }
+    }
+  } else if (to_smem) {
+    const int total = B * chunks, step = nwarps * 32;
+    for (int base = warp_id * 32 + lane; base < total; base += step * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * step;
+        v[u] = i < total ? ldcg16(src + (i / chunks) * src_stride + (i % chunks) * 8) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * step;
+        if (i < total) *reinterpret_cast<uint4*>(xs + (i / chunks) * xs_stride + (i % chunks) * 8) = v[u];
+      }
+    }
+  }
+}
+
+struct EpilogueArgs {
+  void* out;  // bf16 (store / residual in-out / silu) or fp32 logits
+  int64_t out_stride;
+  int rows;   // weight rows (logits: vocabulary)
+  int batch;
+  float* partials;  // logits: one sampling record per row block and batch row
+  const int64_t* state;
+  float temperature;
+  uint64_t seed;
+};
+
+// Row block rb's outputs from the complete fp32 sums acc (lane layout of mma m16n8: rows
+// h*16 + g + 8*(e>>1), batch column 8j + 2t + (e&1)). Reads of the residual use L2-only loads.
+template <int EPI, int NT>
+__device__ __forceinline__ void row_block_epilogue(const float (&acc)[2][NT][4], int rb, int lane,
+                                                   const EpilogueArgs& a) {
+  const int g = lane >> 2, t = lane & 3, B = a.batch;
+  if constexpr (EPI == kGemvStore || EPI == kGemvResidual) {
+    bf16* out = static_cast<bf16*>(a.out);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = rb * 32 + h * 16 + g + 8 * (e >> 1);
+          const int b = 8 * j + 2 * t + (e & 1);
+          if (b >= B || n >= a.rows) continue;
+          bf16* dst = out + b * a.out_stride + n;
+          if constexpr (EPI == kGemvStore) *dst = __float2bfloat16_rn(acc[h][j][e]);
+          else *dst = __float2bfloat16_rn(ldcg_bf16(dst) + bf16_round(acc[h][j][e]));
+        }
+  } else if constexpr (EPI == kGemvSiluMul) {
+    bf16* out = static_cast<bf16*>(a.out);
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int col = rb * 16 + g + 8 * (e >> 1);
+        const int b = 8 * j + 2 * t + (e & 1);
+        if (b >= B) continue;
+        const float gate = bf16_round(acc[0][j][e]);
+        const float up = bf16_round(acc[1][j][e]);
+        const float act = bf16_round(gate / (1.0f + expf(-gate)));
+        out[b * a.out_stride + col] = __float2bfloat16_rn(act * up);
+      }
+  } else {  // fp32 logits + per-row-block sampling records
+    float* logits = static_cast<float*>(a.out);
+    const float temperature =
+        a.state ? __int_as_float(static_cast<int>(a.state[IPE_STATE_TEMPERATURE])) : a.temperature;
+    const uint64_t seed = a.state ? static_cast<uint64_t>(a.state[IPE_STATE_SEED]) : a.seed;
+    const int64_t step = a.state ? a.state[IPE_STATE_STEP] : 0;
+#pragma unroll
+    for (int j = 0; j < NT; ++j)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int b = 8 * j + 2 * t + c;
+        Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const int n = rb * 32 + h * 16 + g + 8 * r;
+            if (b < B && n < a.rows) {
+              const float l = bf16_round(acc[h][j][2 * r + c]);
+              logits[b * a.out_stride + n] = l;
+              Stat y{l, 1.f, n, -INFINITY, 0x7fffffff};
+              if (temperature > 0.f) {
+                y.gs = l / temperature - logf(-logf(uniform01(seed, n, b, step)));
+                y.garg = n;
+              }
+              st = merge(st, y);
+            }
+          }
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) {
+          Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
+                 __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
+                 __shfl_xor_sync(0xffffffffu, st.garg, o)};
+          st = merge(st, y);
+        }
+        if (g == 0 && b < B) {
+          float* rec = a.partials + (static_cast<int64_t>(rb) * B + b) * IPE_PARTIAL_WORDS;
+          rec[0] = st.m;
+          rec[1] = st.s;
+          rec[2] = st.gs;
+          rec[3] = 0.f;
+          rec[4] = __int_as_float(st.arg);
+          rec[5] = __int_as_float(st.garg);
+        }
+      }
+  }
+}
+
+}  // namespace ipe

@@ -47,9 +47,31 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_decode_attention_static_scratch": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, _P]),
     "ipe_prefill_attention": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P]),
     "ipe_gemm": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P]),
+    "ipe_decode_step": (c_int, [ctypes.c_void_p, _P]),
+    "ipe_decode_step_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ipe_state_set": (c_int, [_P, c_int, c_int64, _P]),
     "ipe_state_add": (c_int, [_P, c_int, c_int64, _P]),
 }
+
+
+class LayerDesc(ctypes.Structure):
+    """ipe_layer_desc of include/ipe_b200.h."""
+
+    _fields_ = [(name, c_void_p) for name in (
+        "input_layernorm", "post_attention_layernorm", "q_norm", "k_norm", "qkv_tiles", "o_tiles", "gate_up_tiles",
+        "down_tiles", "k_cache", "v_cache")]
+
+
+class StepDesc(ctypes.Structure):
+    """ipe_decode_step_desc of include/ipe_b200.h."""
+
+    _fields_ = [("layers", c_int), ("hidden", c_int), ("intermediate", c_int), ("q_heads", c_int),
+                ("kv_heads", c_int), ("vocab", c_int), ("capacity", c_int), ("batch", c_int), ("eps", c_float),
+                ("layer_descs", c_void_p), ("embed", c_void_p), ("lm_head_tiles", c_void_p), ("final_norm", c_void_p),
+                ("cos_table", c_void_p), ("sin_table", c_void_p), ("state", c_void_p), ("tokens", c_void_p),
+                ("x", c_void_p), ("qkv", c_void_p), ("attn", c_void_p), ("act", c_void_p), ("logits", c_void_p),
+                ("partials", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+                ("history_tokens", c_void_p), ("history_logprobs", c_void_p), ("history_stride", c_int64)]
 
 
 class NativeUnavailable(RuntimeError):

@@ -86,9 +86,11 @@ class Engine:
         self._v = torch.full(shape, float("nan"), dtype=dtype, device=device)
         self._cos, self._sin = self._model.decode_rotary(capacity)
         self._buf = _model.DecodeBuffers(self._model, batch, capacity)
+        self._layer_descs = _model.layer_descs(self._model, self._k, self._v)
+        self._step_descs: dict[tuple[int, bool], object] = {}
         self._prefill_buf: _model.PrefillBuffers | None = None
-        self._graphs: dict[int, torch.cuda.CUDAGraph] = {}
-        self._eager_steps = 0
+        self._graphs: dict[tuple[int, bool], torch.cuda.CUDAGraph] = {}
+        self._warm: set[tuple[int, bool]] = set()  # step variants already run once outside capture
         self._device_pos = 0  # what state[POS] holds once the queued work has run
         self.batch = 0
         self.length = 0
@@ -146,11 +148,13 @@ class Engine:
         """The generation loop with its results left on the device: (tokens [B, N], logprobs [B, N],
         lengths [B], produced). `after_prefill()` is called once the prefill is queued (timing hook).
 
-        Each iteration queues the fused sampler (it reads the LM head's partial records, writes the
-        token into the history and into the next step's input buffer) and one decode step."""
+        The first token comes from the fused sampler over the prefill's LM-head records; every later
+        one from a decode step that samples its own logits (one kernel per step, replayed from a
+        CUDA graph): the sampled ID goes to the history and becomes the next step's input."""
         device = self._model.device
         stream = torch.cuda.current_stream().cuda_stream
-        lib, state = nat.load(), self._buf.state.data_ptr()
+        lib, buf = nat.load(), self._buf
+        state = buf.state.data_ptr()
         nat.check(lib.ipe_state_set(state, nat.STATE_STEP, 0, stream), "ipe_state_set")
         nat.check(lib.ipe_state_set(state, nat.STATE_SEED, seed & (2**63 - 1), stream), "ipe_state_set")
         nat.check(lib.ipe_state_set(state, nat.STATE_TEMPERATURE, _float_bits(temperature), stream), "ipe_state_set")
@@ -160,15 +164,14 @@ class Engine:
             if after_prefill is not None:
                 after_prefill()
             batch, vocab = self.batch, self.loaded.config.vocab_size
-            tokens = torch.empty((batch, max_new_tokens), dtype=torch.int64, device=device)
-            logprobs = torch.empty((batch, max_new_tokens), dtype=torch.float32, device=device)
+            tokens, logprobs = buf.history_tokens[:batch], buf.history_logprobs[:batch]
+            nat.check(lib.ipe_sample(buf.partials.data_ptr(), buf.logits.data_ptr(), batch, vocab, temperature, state,
+                                     tokens.data_ptr(), logprobs.data_ptr(), tokens.stride(0), buf.tokens.data_ptr(),
+                                     stream), "ipe_sample")
             lengths = torch.full((batch,), max_new_tokens, dtype=torch.int64, device=device)
             stopped = torch.zeros(batch, dtype=torch.bool, device=device)
             produced = max_new_tokens
             for step in range(max_new_tokens):
-                nat.check(lib.ipe_sample(self._buf.partials.data_ptr(), self._buf.logits.data_ptr(), batch, vocab,
-                                         temperature, state, tokens.data_ptr(), logprobs.data_ptr(),
-                                         max_new_tokens, self._buf.tokens.data_ptr(), stream), "ipe_sample")
                 if stops is not None:
                     first = torch.isin(tokens[:, step], stops) & ~stopped
                     lengths = torch.where(first, step + 1, lengths)
@@ -177,26 +180,26 @@ class Engine:
                         produced = step + 1
                         break
                 if step + 1 < max_new_tokens:
-                    self._decode_from_buffer()
+                    self._decode_from_buffer(sample=True)
         finally:
             nat.check(lib.ipe_state_set(state, nat.STATE_TEMPERATURE, 0, stream), "ipe_state_set")
-        return tokens, logprobs, lengths, produced
+        return tokens[:, :max_new_tokens].clone(), logprobs[:, :max_new_tokens].clone(), lengths, produced
 
     def kernel_launches(self, prompt: int, new_tokens: int) -> dict[str, int]:
         """How many library kernels one `generate(prompt, new_tokens)` launches, by phase."""
         layers = self.loaded.config.num_hidden_layers
         prefill = 1 + layers * 8 + 2  # embed; norm, qkv, rope/append, attention, o, norm, gate/up, down; head, state
-        decode = 1 + layers * 5 + 2  # embed; qkv, fused attention, o, gate/up, down; head, advance
+        decode = 1  # the whole step, sampling included, is one kernel (plus a 8-byte memset node)
         return {"prefill": prefill, "decode_step": decode, "sample": 1,
-                "generate": 4 + prefill + new_tokens + (new_tokens - 1) * decode}
+                "generate": 4 + prefill + 1 + (new_tokens - 1) * decode}
 
     # ---------------------------------------------------------------------------------- steps
 
-    def _decode_from_buffer(self) -> None:
+    def _decode_from_buffer(self, sample: bool = False) -> None:
         """A decode step whose input tokens are already in the device token buffer."""
         if self.length == self.capacity:
             raise ValueError(f"decode: all {self.capacity} positions are committed")
-        self._run_decode(self.length)
+        self._run_decode(self.length, sample=sample)
         self.length += 1
 
     def _step(self, token_ids: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor], start: int) -> torch.Tensor:
@@ -250,22 +253,38 @@ class Engine:
                                   c.rms_norm_eps, 0.0, 0, buf.state.data_ptr(), stream), "ipe_lm_head")
         nat.check(lib.ipe_state_add(buf.state.data_ptr(), nat.STATE_POS, 1, stream), "ipe_state_add")
 
-    def _run_decode(self, start: int, batch: int | None = None) -> None:
+    def _launch_step(self, batch: int, sample: bool, stream: int) -> None:
+        """The whole decode step as one kernel (ipe_decode_step)."""
+        import ctypes
+
+        key = (batch, sample)
+        desc = self._step_descs.get(key)
+        if desc is None:
+            desc = _model.step_desc(self._model, self._buf, self._layer_descs, batch, self.capacity, self._cos,
+                                    self._sin, sample)
+            self._step_descs[key] = desc
+        nat.check(nat.load().ipe_decode_step(ctypes.addressof(desc), stream), "ipe_decode_step")
+
+    def _run_decode(self, start: int, batch: int | None = None, sample: bool = False) -> None:
         batch = self.batch if batch is None else batch
         stream = torch.cuda.current_stream().cuda_stream
         if self._device_pos != start:
             nat.check(nat.load().ipe_state_set(self._buf.state.data_ptr(), nat.STATE_POS, start, stream),
                       "ipe_state_set")
-        use_graph = decoder_layer is _BUILTIN_DECODE and self._eager_steps > 0
-        if not use_graph:
+        if decoder_layer is not _BUILTIN_DECODE:
+            # a replaced per-layer hook runs the per-operator kernels eagerly, layer by layer
+            if sample:
+                raise RuntimeError("sampling decode steps need the built-in decode path")
             self._launch_decode(batch, stream)
-            self._eager_steps += 1
+        elif (batch, sample) not in self._warm:
+            self._launch_step(batch, sample, stream)
+            self._warm.add((batch, sample))
         else:
-            graph = self._graphs.get(batch)
+            graph = self._graphs.get((batch, sample))
             if graph is None:
                 graph = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(graph):
-                    self._launch_decode(batch, torch.cuda.current_stream().cuda_stream)
-                self._graphs[batch] = graph
+                    self._launch_step(batch, sample, torch.cuda.current_stream().cuda_stream)
+                self._graphs[(batch, sample)] = graph
             graph.replay()
         self._device_pos = start + 1

@@ -206,6 +206,12 @@ class DecodeBuffers:
         self.linear_workspace = torch.zeros(max(linear, 256), dtype=torch.uint8, device=dev)
         self.state = torch.zeros(nat.STATE_WORDS, dtype=torch.int64, device=dev)
         self.tokens = torch.zeros(batch, dtype=torch.int64, device=dev)
+        # generation history: row b, sampled token s at [b, s] (fixed buffers, so captured steps replay)
+        self.history_tokens = torch.zeros((batch, capacity), dtype=torch.int64, device=dev)
+        self.history_logprobs = torch.zeros((batch, capacity), dtype=torch.float32, device=dev)
+        step_ws = int(lib.ipe_decode_step_workspace(batch, c.num_attention_heads, c.num_key_value_heads, capacity))
+        # grid barrier, attention arrival counters and partial records of the one-kernel decode step
+        self.step_workspace = torch.zeros(step_ws, dtype=torch.uint8, device=dev)
 
 
 def decode_layer(model: PackedModel, index: int, buf: DecodeBuffers, k_layer: torch.Tensor, v_layer: torch.Tensor,
@@ -230,3 +236,39 @@ def decode_layer(model: PackedModel, index: int, buf: DecodeBuffers, k_layer: to
               "ipe_rmsnorm_gate_up_silu")
     nat.check(lib.ipe_linear_residual(buf.act.data_ptr(), p["t_down"], x, batch, c.intermediate_size, c.hidden_size,
                                       ws, wsn, stream), "ipe_linear_residual down_proj")
+
+
+def layer_descs(model: PackedModel, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    """The device array of ipe_layer_desc for a cache pair k / v [layers, batch, kv_heads, capacity, 128]."""
+    import ctypes
+
+    descs = (nat.LayerDesc * len(model.layers))()
+    for i, layer in enumerate(model.layers):
+        p = layer.ptr
+        descs[i] = nat.LayerDesc(p["in_norm"], p["post_norm"], p["q_norm"], p["k_norm"], p["t_qkv"], p["t_o"],
+                                 p["t_gate_up"], p["t_down"], k[i].data_ptr(), v[i].data_ptr())
+    raw = torch.frombuffer(bytearray(ctypes.string_at(ctypes.addressof(descs), ctypes.sizeof(descs))),
+                           dtype=torch.uint8)
+    return raw.to(model.device)
+
+
+def step_desc(model: PackedModel, buf: DecodeBuffers, descs: torch.Tensor, batch: int, capacity: int,
+              cos: torch.Tensor, sin: torch.Tensor, sample: bool):
+    """ipe_decode_step_desc of one decode step over the engine's fixed buffers."""
+    c = model.config
+    d = nat.StepDesc()
+    d.layers, d.hidden, d.intermediate = c.num_hidden_layers, c.hidden_size, c.intermediate_size
+    d.q_heads, d.kv_heads, d.vocab, d.capacity, d.batch = (c.num_attention_heads, c.num_key_value_heads,
+                                                           c.vocab_size, capacity, batch)
+    d.eps = c.rms_norm_eps
+    d.layer_descs = descs.data_ptr()
+    d.embed, d.lm_head_tiles, d.final_norm = model.embed.data_ptr(), model.t_lm_head.data_ptr(), model.final_norm.data_ptr()
+    d.cos_table, d.sin_table = cos.data_ptr(), sin.data_ptr()
+    d.state, d.tokens = buf.state.data_ptr(), buf.tokens.data_ptr()
+    d.x, d.qkv, d.attn, d.act = buf.x.data_ptr(), buf.qkv.data_ptr(), buf.attn.data_ptr(), buf.act.data_ptr()
+    d.logits, d.partials = buf.logits.data_ptr(), buf.partials.data_ptr()
+    d.workspace, d.workspace_bytes = buf.step_workspace.data_ptr(), buf.step_workspace.numel()
+    if sample:
+        d.history_tokens, d.history_logprobs = buf.history_tokens.data_ptr(), buf.history_logprobs.data_ptr()
+        d.history_stride = buf.history_tokens.shape[1]
+    return d

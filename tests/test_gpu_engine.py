@@ -245,13 +245,25 @@ def test_decode_steps_never_synchronize_or_grow_the_allocator(models):
     assert torch.cuda.memory_reserved() == reserved
 
 
-def test_graph_replay_equals_eager_launches(models, monkeypatch):
+def test_one_kernel_step_agrees_with_the_per_operator_kernels(models, monkeypatch):
+    """The graph-replayed one-kernel decode step against the per-operator kernels run eagerly (a
+    replaced layer hook selects them): the same math summed in a different order, so within a few
+    bf16 ulps of the logits, and the greedy choices agree."""
     _, gpu = models("small")
     ids = torch.randint(0, 2048, (2, 20), generator=torch.Generator().manual_seed(12))
-    graphed = teacher_forced(Engine(gpu, batch=2, capacity=24), ids, 6)
+    stepped = teacher_forced(Engine(gpu, batch=2, capacity=24), ids, 6)
     monkeypatch.setattr(engine_module, "decoder_layer", lambda *a, **k: engine_module._BUILTIN_DECODE(*a, **k))
-    eager = teacher_forced(Engine(gpu, batch=2, capacity=24), ids, 6)
-    assert torch.equal(graphed, eager)
+    per_op = teacher_forced(Engine(gpu, batch=2, capacity=24), ids, 6)
+    assert ((stepped - per_op).abs() <= 4 * 2 ** -8 * per_op.abs() + 0.05).all()
+    assert (stepped.argmax(-1) == per_op.argmax(-1)).float().mean() > 0.9
+
+
+def test_one_kernel_steps_are_deterministic(models):
+    _, gpu = models("mqa")
+    ids = torch.randint(0, 512, (1, 30), generator=torch.Generator().manual_seed(13))
+    a = teacher_forced(Engine(gpu, batch=1, capacity=32), ids, 5)
+    b = teacher_forced(Engine(gpu, batch=1, capacity=32), ids, 5)
+    assert torch.equal(a, b)
 
 
 # --------------------------------------------------------------- Qwen3-1.7B, 28 layers
