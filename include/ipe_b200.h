@@ -215,7 +215,8 @@ int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epi
 
 /* ------------------------------------------------------------------ whole decode step */
 
-/* One decoder layer's operands for ipe_decode_step (device pointers). */
+/* One decoder layer's operands for ipe_decode_step (device pointers, each 16-byte aligned; the
+ * array lives in device memory, so the host entry point cannot check them). */
 typedef struct {
   const void* input_layernorm;          /* bf16 [hidden]                                    */
   const void* post_attention_layernorm; /* bf16 [hidden]                                    */
@@ -252,7 +253,18 @@ typedef struct {
   int64_t* history_tokens;           /* nullable: sample the next token into [b*stride+step] */
   float* history_logprobs;
   int64_t history_stride;
+  uint64_t* trace;                   /* nullable: per-CTA phase timestamps, see below         */
 } ipe_decode_step_desc;
+
+/* Step trace (when desc.trace is set): CTA c writes globaltimer nanoseconds to
+ * trace[c * IPE_TRACE_WORDS(layers) + i]: i = 0 kernel start; for grid barrier j = 1 .. 5*layers+2
+ * (embedding, then per layer after QKV, attention, o_proj, gate/up, down_proj, then the LM head),
+ * i = 5j-4 its arrival, 5j-3 its release, and for the phase that follows it: 5j-2 activations
+ * staged, 5j-1 first weight tile (attention: first item) ready, 5j last weight tile ready (last
+ * item done); the last word the CTA's end. Words of events that did not happen are left as they
+ * were. The array needs ipe_decode_step_grid() * IPE_TRACE_WORDS(layers) words. */
+#define IPE_TRACE_WORDS(layers) (25 * (layers) + 12)
+int ipe_decode_step_grid(void);
 
 /* One whole decode step (embedding, all layers, final norm, LM head, and the sampler when
  * history_tokens is set) as ONE persistent cooperative kernel, one CTA per SM: a producer warp

@@ -8,6 +8,7 @@
 #include "common.cuh"
 #include "decode_attention.cuh"
 #include "launch.h"
+#include "tensor_map.h"
 
 namespace ipe {
 namespace {
@@ -147,20 +148,21 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
 }
 
 // ------------------------------------------------------------------------------------------
-// Fused decode-step attention (decode_attention.cuh): one CTA per (chunk, KV head, batch row).
+// Fused decode-step attention (decode_attention.cuh): one CTA per (split, KV head, batch row).
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) fused_decode_kernel(const FusedArgs a) {
   extern __shared__ float scratch[];
   pdl_trigger();
   pdl_wait();
-  const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int pos = a.state ? static_cast<int>(a.state[IPE_STATE_POS]) : a.start;
   if (pos < 0 || pos >= a.capacity) {
-    if (threadIdx.x == 0 && chunk == 0) report(a.err, kErrPositionRange);
+    if (threadIdx.x == 0 && split == 0) report(a.err, kErrPositionRange);
     return;
   }
-  if (chunk * kAttnChunk > pos) return;
-  attention_item<G>(a, chunk, kvh, b, pos, AttnSmem<G>(scratch, a.chunks_max), threadIdx.x);
+  const AttnSplit sp = attn_split(pos, a.max_splits);
+  if (split >= sp.splits) return;
+  attention_item<G>(a, split, kvh, b, pos, sp, AttnSmem<G>(scratch), threadIdx.x);
 }
 
 template <int G>
@@ -198,20 +200,20 @@ cudaError_t launch_decode_attention(const void* q, const void* k, const void* v,
 }
 
 size_t fused_decode_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity) {
-  const int chunks_max = (capacity + kAttnChunk - 1) / kAttnChunk;
+  (void)capacity;  // records are per split, and splits are bounded by kAttnSplitsMax
   const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int) + 255) / 256 * 256;
-  return counters + static_cast<size_t>(batch) * q_heads * chunks_max * kAttnRecord * sizeof(float);
+  return counters + static_cast<size_t>(batch) * q_heads * kAttnSplitsMax * kAttnRecord * sizeof(float);
 }
 
 template <int G>
 cudaError_t launch_fused(const FusedArgs& a, int batch, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(attn_smem_floats<G>(a.chunks_max)) * sizeof(float);
+  const size_t smem = static_cast<size_t>(attn_smem_floats<G>()) * sizeof(float);
   auto kernel = fused_decode_kernel<G>;
   if (smem > 40 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e != cudaSuccess) return e;
   }
-  return launch_pdl(kernel, dim3(a.chunks_max, a.kv_heads, batch), dim3(kAttnThreads), smem, stream, a);
+  return launch_pdl(kernel, dim3(a.max_splits, a.kv_heads, batch), dim3(kAttnThreads), smem, stream, a);
 }
 
 cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, const void* k_norm, const void* cos_t,
@@ -232,7 +234,7 @@ cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, c
   a.q_heads = q_heads;
   a.kv_heads = kv_heads;
   a.capacity = capacity;
-  a.chunks_max = (capacity + kAttnChunk - 1) / kAttnChunk;
+  a.max_splits = attn_max_splits(2 * sm_count(), batch, kv_heads);
   a.eps = eps;
   a.err = err;
   a.counters = static_cast<int*>(workspace);

@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "launch.h"
+#include "tensor_map.h"
 
 namespace ipe {
 size_t decode_attention_workspace_bytes(int batch, int q_heads, int capacity);
@@ -331,12 +332,18 @@ size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capac
   return ipe::decode_step_workspace_bytes(batch, q_heads, kv_heads, capacity);
 }
 
+int ipe_decode_step_grid(void) { return ipe::sm_count(); }
+
 int ipe_decode_step(const ipe_decode_step_desc* d, void* stream) {
   if (!d) return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: null descriptor");
   if (!d->layer_descs || !d->embed || !d->lm_head_tiles || !d->final_norm || !d->cos_table || !d->sin_table ||
       !d->state || !d->tokens || !d->x || !d->qkv || !d->attn || !d->act || !d->logits || !d->partials ||
       !d->workspace)
     return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: null pointer in the descriptor");
+  const void* const operands[] = {d->embed, d->lm_head_tiles, d->final_norm, d->cos_table, d->sin_table, d->x,
+                                  d->qkv,   d->attn,          d->act,        d->logits,    d->workspace};
+  for (const void* p : operands)
+    if (!aligned16(p)) return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: descriptor pointers must be 16-byte aligned");
   if (d->layers < 1 || d->batch < 1 || d->batch > 16 || d->capacity < 1 || d->vocab < 1 || d->q_heads < 1 ||
       d->kv_heads < 1 || d->q_heads % d->kv_heads)
     return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: bad sizes");

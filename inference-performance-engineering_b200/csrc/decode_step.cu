@@ -5,19 +5,22 @@
 //
 // Why one kernel: every weight byte of the step is known before the step starts, so the weight
 // stream does not depend on activations. Each CTA (one per SM, cooperative launch) has a producer
-// warp that walks its share of ALL phases' decode tiles back to back with 8 KB bulk copies into
-// per-consumer-warp shared-memory slots, and never waits for a phase boundary; the HBM stream
-// continues across the whole step. The 4 consumer warps wait only where the data requires it: at
-// a bounded-spin grid barrier after each phase (the next phase needs the full activation vector),
+// warp that walks its share of ALL phases' decode tiles back to back with bulk copies into
+// per-consumer-warp shared-memory slots and never waits for a phase boundary; ahead of those
+// copies it issues L2 prefetches of the same units, of the K / V rows its attention items will
+// read, and of the norm weights. The 4 consumer warps wait only where the data requires it: at a
+// bounded-spin grid barrier after each phase (the next phase needs the full activation vector),
 // then they stage that vector in shared memory and consume tiles that are usually already there.
 //
-// Work split: a phase's row blocks (32 weight rows each, whole K, no split-K) are dealt
-// round-robin over the CTAs, continuing where the previous phase stopped so every CTA streams
-// the same number of row blocks per step; within a CTA a row block's tiles go round-robin to the
+// Work split: a phase's units (a 32-row block, or a 16-row half block where that evens out the
+// bytes per CTA, always over the whole K: no split-K) are dealt round-robin over the CTAs,
+// continuing where the previous phase stopped; within a CTA a unit's tiles go round-robin to the
 // consumer warps, whose partial sums are reduced in a fixed order through shared memory
-// (deterministic). Every spin (grid barrier, mbarrier) is bounded; a timeout sets the device error
-// word and an abort flag and the kernel winds down.
+// (deterministic). Attention runs as (split, KV head, row) items over the CTAs. Every spin (grid
+// barrier, mbarrier) is bounded; a timeout sets the device error word and an abort flag and the
+// kernel winds down.
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -31,8 +34,8 @@ namespace ipe {
 namespace {
 
 constexpr int kConsumers = 4;
-constexpr int kSlotsPerWarp = 4;
-constexpr int kStages = kConsumers * kSlotsPerWarp;  // 16 x 8 KB = 128 KB of weights in flight
+constexpr int kMaxSlotsPerWarp = 8;
+constexpr int kMaxStages = kConsumers * kMaxSlotsPerWarp;  // 8 KB slots (bounded by shared memory)
 constexpr int kThreads = 32 * (kConsumers + 1);
 constexpr int kCThreads = 32 * kConsumers;
 constexpr int kPad = 32;
@@ -45,7 +48,11 @@ struct StepArgs {
   int* attn_counters;
   float* attn_records;
   int* err;
-  int chunks_max;
+  int slots;                // ring slots per consumer warp
+  int max_splits;           // attention splits per (row, KV head)
+  unsigned prefetch_bytes;  // how far the L2 prefetch runs ahead of the shared-memory copies
+  int evict_first;          // weight copies mark their L2 lines evict-first
+  int halves;               // half-row-block units allowed
 };
 
 __device__ __forceinline__ void consumers_sync() {
@@ -59,9 +66,11 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 }
 
 // Grid barrier among the consumer warps of all CTAs. Returns false when the step is aborted.
-__device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort_smem) {
+// trace (this CTA's row of the step trace, or null) receives the arrival and release times.
+__device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort_smem, uint64_t* trace) {
   consumers_sync();
   if (tid == 0) {
+    if (trace) trace[1 + 5 * (index - 1)] = globaltimer_ns();
     __threadfence();
     atomicAdd(&a.grid_bar[0], 1u);
     const unsigned target = index * gridDim.x;
@@ -85,30 +94,60 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
       __nanosleep(64);
     }
     __threadfence();
+    if (trace) trace[2 + 5 * (index - 1)] = globaltimer_ns();
   }
   consumers_sync();
   return *abort_smem == 0;
 }
 
-// First row block of this CTA in a phase that starts dealing at `cursor`.
-__device__ __forceinline__ int first_row_block(int cursor) {
+// First unit of this CTA in a phase that starts dealing at `cursor`.
+__device__ __forceinline__ int first_unit(int cursor) {
   const int g = static_cast<int>(gridDim.x);
   return (static_cast<int>(blockIdx.x) - cursor % g + g) % g;
 }
 
+// A weight phase as units dealt round-robin over the CTAs: a unit is one row block (32 rows, whole
+// K, 8 KB tiles) or, when that lowers the most bytes any CTA streams in the phase, one 16-row half
+// of a row block (4 KB half tiles).
 struct PhaseShape {
   const unsigned char* tiles;
-  int row_blocks;
-  int ku;  // tiles per row block
+  int units;
+  int ku;  // tiles per unit
+  bool half;
+};
+
+__device__ __forceinline__ PhaseShape make_phase(const void* tiles, int row_blocks, int ku, bool may_halve) {
+  const int g = static_cast<int>(gridDim.x);
+  const bool half = may_halve && (2 * row_blocks + g - 1) / g < 2 * ((row_blocks + g - 1) / g);
+  return {static_cast<const unsigned char*>(tiles), half ? 2 * row_blocks : row_blocks, ku, half};
+}
+
+// Slot bookkeeping of one consumer warp's ring share: slot index and how often it wrapped.
+struct SlotCursor {
+  int slot = 0, fill = 0;
+  __device__ __forceinline__ void advance(int slots) {
+    if (++slot == slots) {
+      slot = 0;
+      ++fill;
+    }
+  }
+};
+
+// Position of a walk over this CTA's units of the step, in stream order.
+struct UnitWalk {
+  int layer = 0, kind = 0, cursor = 0, unit = 0;
+  bool in_phase = false, done = false;
+  PhaseShape ph{};
 };
 
 template <int NT, int G, bool ACT_SMEM>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
+  const int S = a.slots;
   unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kStages * kTileBytes);
-  uint64_t* empty = full + kStages;
-  float* rstd = reinterpret_cast<float*>(empty + kStages);  // [16]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kConsumers * S * kTileBytes);
+  uint64_t* empty = full + kMaxStages;
+  float* rstd = reinterpret_cast<float*>(empty + kMaxStages);  // [16]
   int* abort_smem = reinterpret_cast<int*>(rstd + 16);
   float* red = reinterpret_cast<float*>(abort_smem + 4);  // [kConsumers][32][8 * NT]
   float* scratch = red + kConsumers * 32 * 8 * NT;        // activations or attention scratch
@@ -121,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   const int G_ = static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < kConsumers * S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -130,49 +169,127 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   }
   __syncthreads();
 
+  // kind: 0 QKV, 1 o_proj, 2 gate/up, 3 down_proj; layer == layers: the LM head.
   auto phase_shape = [&](int layer, int kind) -> PhaseShape {
-    if (layer == d.layers) return {static_cast<const unsigned char*>(d.lm_head_tiles), (d.vocab + 31) / 32, H / kTileK};
+    if (layer == d.layers) return make_phase(d.lm_head_tiles, (d.vocab + 31) / 32, H / kTileK, false);
     const ipe_layer_desc& L = d.layer_descs[layer];
     switch (kind) {
-      case 0: return {static_cast<const unsigned char*>(L.qkv_tiles), QKV / 32, H / kTileK};
-      case 1: return {static_cast<const unsigned char*>(L.o_tiles), H / 32, Q / kTileK};
-      case 2: return {static_cast<const unsigned char*>(L.gate_up_tiles), I / 16, H / kTileK};
-      default: return {static_cast<const unsigned char*>(L.down_tiles), H / 32, I / kTileK};
+      case 0: return make_phase(L.qkv_tiles, QKV / 32, H / kTileK, a.halves != 0);
+      case 1: return make_phase(L.o_tiles, H / 32, Q / kTileK, a.halves != 0);
+      case 2: return make_phase(L.gate_up_tiles, I / 16, H / kTileK, false);
+      default: return make_phase(L.down_tiles, H / 32, I / kTileK, a.halves != 0);
     }
+  };
+
+  // Next unit of a walk (w.ph and w.unit describe it); entered_layer is set to the layer whose QKV
+  // phase the walk just entered (else -1).
+  auto next_unit = [&](UnitWalk& w, int& entered_layer) -> bool {
+    entered_layer = -1;
+    while (!w.done) {
+      if (!w.in_phase) {
+        w.ph = phase_shape(w.layer, w.kind);
+        w.unit = first_unit(w.cursor);
+        w.in_phase = true;
+        if (w.kind == 0 && w.layer < d.layers) entered_layer = w.layer;
+      } else {
+        w.unit += G_;
+      }
+      if (w.unit < w.ph.units) return true;
+      w.cursor = (w.cursor + w.ph.units) % G_;
+      w.in_phase = false;
+      if (w.layer == d.layers) w.done = true;
+      else if (++w.kind == 4) {
+        w.kind = 0;
+        ++w.layer;
+      }
+    }
+    return false;
   };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
+    // Bulk copies of this CTA's tiles into the consumer warps' ring slots (tile t of a unit to
+    // warp t % 4), and, prefetch_bytes ahead of them, L2 prefetches of the same units plus the
+    // K / V rows this CTA's attention items of each layer will read. The per-tile path is kept
+    // short: one thread issues every copy of the SM.
     if (lane == 0) {
       const uint32_t ring_base = smem_addr(ring);
-      int kcount[kConsumers] = {0, 0, 0, 0};
-      int cursor = 0;
-      bool ok = true;
-      for (int layer = 0; layer <= d.layers && ok; ++layer) {
-        for (int kind = 0; kind < (layer == d.layers ? 1 : 4) && ok; ++kind) {
-          const PhaseShape ph = phase_shape(layer, kind);
-          for (int rb = first_row_block(cursor); rb < ph.row_blocks && ok; rb += G_) {
-            const unsigned char* src = ph.tiles + static_cast<int64_t>(rb) * ph.ku * kTileBytes;
-            for (int t0 = 0; t0 < ph.ku && ok; t0 += kConsumers) {
-#pragma unroll
-              for (int w = 0; w < kConsumers; ++w) {
-                const int t = t0 + w;
-                if (t >= ph.ku || !ok) continue;
-                const int k = kcount[w]++;
-                const int slot = w * kSlotsPerWarp + (k & (kSlotsPerWarp - 1));
-                const int fill = k / kSlotsPerWarp;
-                if (fill > 0 && !mbar_wait(&empty[slot], (fill - 1) & 1, a.err)) {
-                  ok = false;
-                  continue;
-                }
-                mbar_expect_tx(&full[slot], kTileBytes);
-                bulk_copy(ring_base + slot * kTileBytes, src + static_cast<int64_t>(t) * kTileBytes, kTileBytes,
-                          &full[slot]);
-              }
-            }
+      const uint64_t policy = evict_first_policy();
+      const int pos = static_cast<int>(d.state[IPE_STATE_POS]);
+      if (pos < 0 || pos >= d.capacity) return;  // the consumers leave too; nothing was issued
+      const AttnSplit sp = attn_split(pos, a.max_splits);
+      auto prefetch_kv = [&](int layer) {
+        const ipe_layer_desc& L = d.layer_descs[layer];
+        // the layer's norm weights too (the stages that read them are on the critical path); a
+        // bulk prefetch needs a 16-byte aligned start, so an unaligned vector is left to the loads
+        auto prefetch_vec = [&](const void* p, uint32_t bytes) {
+          if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) prefetch_l2(p, bytes);
+        };
+        prefetch_vec(L.input_layernorm, static_cast<uint32_t>(H) * 2u);
+        prefetch_vec(L.post_attention_layernorm, static_cast<uint32_t>(H) * 2u);
+        prefetch_vec(L.q_norm, 256u);
+        prefetch_vec(L.k_norm, 256u);
+        if (layer == d.layers - 1) prefetch_vec(d.final_norm, static_cast<uint32_t>(H) * 2u);
+        const int items = sp.splits * d.kv_heads * B;
+        for (int it = static_cast<int>(blockIdx.x); it < items; it += G_) {
+          const int split = it % sp.splits, rest = it / sp.splits;  // rest = row * kv_heads + head
+          const int begin = split * sp.span, end = min(begin + sp.span, pos + 1);
+          const int64_t row0 = static_cast<int64_t>(rest) * d.capacity + begin;
+          for (int k0 = 0; k0 < end - begin; k0 += 64) {  // 64 rows = 16 KB a prefetch
+            const uint32_t bytes = static_cast<uint32_t>(min(64, end - begin - k0)) * 256u;
+            prefetch_l2(static_cast<const bf16*>(L.k_cache) + (row0 + k0) * 128, bytes);
+            prefetch_l2(static_cast<const bf16*>(L.v_cache) + (row0 + k0) * 128, bytes);
           }
-          cursor = (cursor + ph.row_blocks) % G_;
         }
+      };
+      // A unit's tiles are one contiguous range of ku whole tiles (a half unit reads half of each).
+      auto prefetch_unit = [&](const UnitWalk& w) {
+        const int rb = w.ph.half ? w.unit >> 1 : w.unit;
+        const unsigned char* base = w.ph.tiles + static_cast<int64_t>(rb) * w.ph.ku * kTileBytes;
+        for (int t = 0; t < w.ph.ku; t += 8) {  // 8 tiles = 64 KB a prefetch
+          const uint32_t bytes = static_cast<uint32_t>(min(8, w.ph.ku - t)) * kTileBytes;
+          prefetch_l2(base + static_cast<int64_t>(t) * kTileBytes, bytes);
+        }
+      };
+      UnitWalk main_walk, ahead;
+      uint64_t issued = 0, prefetched = 0;
+      SlotCursor sc[kConsumers];
+      bool ok = true;
+      int entered;
+      while (ok && next_unit(main_walk, entered)) {
+        const PhaseShape& ph = main_walk.ph;
+        const uint32_t bytes = ph.half ? kTileBytes / 2 : kTileBytes;
+        while (prefetched < issued + a.prefetch_bytes) {
+          int player;
+          if (!next_unit(ahead, player)) break;
+          if (player >= 0) prefetch_kv(player);
+          prefetch_unit(ahead);
+          prefetched += static_cast<uint64_t>(ahead.ph.ku) * (ahead.ph.half ? kTileBytes / 2 : kTileBytes);
+        }
+        const int rb = ph.half ? main_walk.unit >> 1 : main_walk.unit;
+        const unsigned char* src = ph.tiles + static_cast<int64_t>(rb) * ph.ku * kTileBytes +
+                                   (ph.half ? (main_walk.unit & 1) * (kTileBytes / 2) : 0);
+        for (int t0 = 0; t0 < ph.ku && ok; t0 += kConsumers) {
+#pragma unroll
+          for (int w = 0; w < kConsumers; ++w) {
+            const int t = t0 + w;
+            if (t >= ph.ku || !ok) continue;
+            const int slot = w * S + sc[w].slot;
+            if (sc[w].fill > 0 && !mbar_wait(&empty[slot], (sc[w].fill - 1) & 1, a.err)) {
+              ok = false;
+              continue;
+            }
+            mbar_expect_tx(&full[slot], bytes);
+            if (a.evict_first)
+              bulk_copy_hint(ring_base + slot * kTileBytes, src + static_cast<int64_t>(t) * kTileBytes, bytes,
+                             &full[slot], policy);
+            else
+              bulk_copy(ring_base + slot * kTileBytes, src + static_cast<int64_t>(t) * kTileBytes, bytes,
+                        &full[slot]);
+            sc[w].advance(S);
+          }
+        }
+        issued += static_cast<uint64_t>(ph.ku) * bytes;
       }
     }
     return;
@@ -181,9 +298,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   // -------------------------------------------------------------------- consumers
   const int cw = warp - 1, tid = threadIdx.x - 32;
   const int g = lane >> 2, t = lane & 3;
-  int kcount = 0, cursor = 0;
+  SlotCursor mine;
+  int cursor = 0;
   unsigned barrier_index = 0;
   int64_t* state = d.state;
+  uint64_t* trace = d.trace ? d.trace + static_cast<int64_t>(blockIdx.x) * IPE_TRACE_WORDS(d.layers) : nullptr;
+  if (trace && tid == 0) trace[0] = globaltimer_ns();
+  // trace word k (2: staged, 3: first tile ready, 4: last tile ready) of the current phase
+  auto mark = [&](int k) {
+    if (trace && tid == 0) trace[1 + 5 * (barrier_index - 1) + k] = globaltimer_ns();
+  };
 
   // Embedding: x[b] = embed[tokens[b]] (out-of-range IDs give zeros and set device error 1).
   {
@@ -198,62 +322,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       *reinterpret_cast<uint4*>(x + static_cast<int64_t>(b) * H + v * 8) = val;
     }
   }
-  if (!grid_sync(a, ++barrier_index, tid, abort_smem)) return;
+  if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
 
   // Stage the activation rows of a phase (optionally RMS-normalised) in shared memory; without
   // shared staging only the RMS scales are kept and tiles read activations from global memory.
   auto stage = [&](const bf16* src, const bf16* norm_w, int K) {
-    for (int b = cw; b < B; b += kConsumers) {
-      const bf16* xr = src + static_cast<int64_t>(b) * K;
-      float r = 1.f;
-      if (norm_w) {
-        float ss = 0.f;
-        for (int c = lane; c < K / 8; c += 32) {
-          float f[8];
-          unpack8(ldcg16(xr + c * 8), f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
-        }
-        ss = warp_sum(ss);
-        r = rsqrtf(ss / static_cast<float>(K) + d.eps);
-        if (lane == 0) rstd[b] = r;
-      }
-      if constexpr (ACT_SMEM) {
-        for (int c = lane; c < K / 8; c += 32) {
-          uint4 v = ldcg16(xr + c * 8);
-          if (norm_w) {
-            float f[8], wf[8];
-            unpack8(v, f);
-            unpack8(ldg16(norm_w + c * 8), wf);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * r);
-            v = pack8(f);
-          }
-          *reinterpret_cast<uint4*>(xs + b * (K + kPad) + c * 8) = v;
-        }
-      }
-    }
+    stage_rows(src, K, norm_w, d.eps, B, K, xs, K + kPad, rstd, cw, kConsumers, lane, ACT_SMEM);
     consumers_sync();
+    mark(2);
   };
 
-  // One weight phase: this CTA's row blocks, tiles round-robin over the consumer warps.
+  // One weight phase: this CTA's units, tiles round-robin over the consumer warps.
   auto run_phase = [&](auto epi_tag, const PhaseShape& ph, const bf16* src, const bf16* norm_w, int K,
                        const EpilogueArgs& ea) -> bool {
     constexpr int EPI = decltype(epi_tag)::value;
     float my_rstd[NT];
 #pragma unroll
     for (int j = 0; j < NT; ++j) my_rstd[j] = (!ACT_SMEM && norm_w && 8 * j + g < B) ? rstd[8 * j + g] : 1.f;
-    bool ok = true;
-    for (int rb = first_row_block(cursor); rb < ph.row_blocks; rb += G_) {
+    bool ok = true, first = true;
+    for (int u = first_unit(cursor); u < ph.units; u += G_) {
       float acc[2][NT][4];
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int j = 0; j < NT; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0.f;
       for (int tt = cw; tt < ph.ku && ok; tt += kConsumers) {
-        const int k = kcount++;
-        const int slot = cw * kSlotsPerWarp + (k & (kSlotsPerWarp - 1));
-        const int fill = k / kSlotsPerWarp;
+        const int slot = cw * S + mine.slot;
         const int k0 = tt * kTileK;
         uint4 xv[4][NT];
 #pragma unroll
@@ -279,22 +373,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
               xv[c][j] = raw;
             }
           }
-        if (!mbar_wait(&full[slot], fill & 1, a.err)) {
+        if (!mbar_wait(&full[slot], mine.fill & 1, a.err)) {
           ok = false;
           break;
         }
-        consume_tile<NT>(acc, smem_addr(ring + slot * kTileBytes), xv, g, t);
+        if (trace) {
+          if (first) mark(3);
+          mark(4);
+          first = false;
+        }
+        if (ph.half) consume_half<NT>(acc, smem_addr(ring + slot * kTileBytes), xv, g, t);
+        else consume_tile<NT>(acc, smem_addr(ring + slot * kTileBytes), xv, g, t);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[slot]);
+        mine.advance(S);
+      }
+      if (ph.half) {  // the two column chains of a half unit
+#pragma unroll
+        for (int j = 0; j < NT; ++j)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[0][j][e] += acc[1][j][e];
       }
       // Fixed-order reduction of the warps' partial sums, then the epilogue by warp 0.
-      float* mine = red + (cw * 32 + lane) * 8 * NT;
+      float* part = red + (cw * 32 + lane) * 8 * NT;
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int j = 0; j < NT; ++j)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) mine[(h * NT + j) * 4 + e] = acc[h][j][e];
+          for (int e = 0; e < 4; ++e) part[(h * NT + j) * 4 + e] = acc[h][j][e];
       consumers_sync();
       if (cw == 0) {
 #pragma unroll
@@ -307,12 +414,17 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
 #pragma unroll
               for (int e = 0; e < 4; ++e) acc[h][j][e] += other[(h * NT + j) * 4 + e];
         }
-        row_block_epilogue<EPI, NT>(acc, rb, lane, ea);
+        if (ph.half) {
+          if constexpr (EPI == kGemvStore || EPI == kGemvResidual)
+            row_block_epilogue<EPI, NT>(acc, u >> 1, lane, ea, u & 1, 1);
+        } else {
+          row_block_epilogue<EPI, NT>(acc, u, lane, ea);
+        }
       }
       consumers_sync();
       if (!ok) return false;
     }
-    cursor = (cursor + ph.row_blocks) % G_;
+    cursor = (cursor + ph.units) % G_;
     return true;
   };
 
@@ -330,6 +442,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     if (blockIdx.x == 0 && tid == 0) report(a.err, kErrPositionRange);
     return;  // every CTA sees the same position and leaves before the next barrier
   }
+  const AttnSplit sp = attn_split(pos, a.max_splits);
 
   for (int layer = 0; layer < d.layers; ++layer) {
     const ipe_layer_desc& L = d.layer_descs[layer];
@@ -338,8 +451,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     if (!run_phase(EpiStore{}, phase_shape(layer, 0), x, static_cast<const bf16*>(L.input_layernorm), H,
                    EpilogueArgs{qkv, QKV, QKV, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem)) return;
-    // attention: items (chunk, KV head, row) over the CTAs
+    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
+    // attention: items (split, KV head, row) over the CTAs
     {
       FusedArgs fa{};
       fa.qkv = qkv;
@@ -355,43 +468,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       fa.q_heads = d.q_heads;
       fa.kv_heads = d.kv_heads;
       fa.capacity = d.capacity;
-      fa.chunks_max = a.chunks_max;
+      fa.max_splits = a.max_splits;
       fa.eps = d.eps;
       fa.err = a.err;
-      const int chunks = pos / kAttnChunk + 1;
-      const int items = chunks * d.kv_heads * B;
-      const AttnSmem<G> sm(scratch, a.chunks_max);
+      const int items = sp.splits * d.kv_heads * B;
+      const AttnSmem<G> sm(scratch);
       for (int it = static_cast<int>(blockIdx.x); it < items; it += G_) {
-        const int chunk = it % chunks, rest = it / chunks;
-        attention_item<G>(fa, chunk, rest % d.kv_heads, rest / d.kv_heads, pos, sm, tid);
+        const int split = it % sp.splits, rest = it / sp.splits;
+        // the first item's milestones: K / V requested and q ready, scores and P.V done, merged
+        fa.trace = trace && it == static_cast<int>(blockIdx.x) ? trace + 1 + 5 * (barrier_index - 1) + 2 : nullptr;
+        attention_item<G>(fa, split, rest % d.kv_heads, rest / d.kv_heads, pos, sp, sm, tid);
+        mark(4);
       }
     }
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem)) return;
+    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
     // o_proj + residual
     stage(attn, nullptr, Q);
     if (!run_phase(EpiResidual{}, phase_shape(layer, 1), attn, nullptr, Q,
                    EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem)) return;
+    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
     // post-attention RMSNorm + gate/up + SiLU * up
     stage(x, static_cast<const bf16*>(L.post_attention_layernorm), H);
     if (!run_phase(EpiSilu{}, phase_shape(layer, 2), x, static_cast<const bf16*>(L.post_attention_layernorm), H,
                    EpilogueArgs{act, I, 2 * I, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem)) return;
+    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
     // down_proj + residual
     stage(act, nullptr, I);
     if (!run_phase(EpiResidual{}, phase_shape(layer, 3), act, nullptr, I,
                    EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem)) return;
+    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
   }
   // final RMSNorm + tied LM head: fp32 logits and one sampling record per 32 vocabulary rows
   stage(x, static_cast<const bf16*>(d.final_norm), H);
   if (!run_phase(EpiLogits{}, phase_shape(d.layers, 0), x, static_cast<const bf16*>(d.final_norm), H,
                  EpilogueArgs{d.logits, d.vocab, d.vocab, B, d.partials, state, 0.f, 0}))
     return;
-  if (!grid_sync(a, ++barrier_index, tid, abort_smem)) return;
+  if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
+  if (trace && tid == 0) trace[IPE_TRACE_WORDS(d.layers) - 1] = globaltimer_ns();
   if (blockIdx.x != 0) return;
 
   // Sampling (CTA 0): token and untempered log-probability per row, fed back as the next input.
@@ -429,6 +545,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   }
 }
 
+
 template <int NT, int G, bool ACT>
 cudaError_t launch_variant(const StepArgs& a, size_t smem, cudaStream_t stream) {
   auto kernel = decode_step_kernel<NT, G, ACT>;
@@ -463,33 +580,57 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
   }
 }
 
-size_t fixed_smem(int nt) {
-  return 1024 + static_cast<size_t>(kStages) * kTileBytes + 2 * kStages * 8 + 16 * 4 + 16 +
+// Tuning of the weight stream, fixed per process (measured on B200 with Qwen3-1.7B at batch 1, a
+// 512-token context: these defaults gave the shortest step): ring slots per consumer warp
+// (IPE_STEP_SLOTS, 4), the L2 prefetch distance per CTA in KB (IPE_STEP_PREFETCH_KB, 128; larger
+// distances lengthened the latency-bound phases), weight copies marked L2 evict-first
+// (IPE_STEP_EVICT_FIRST, 1), and half-row-block units (IPE_STEP_HALF, 1).
+struct StepTuning {
+  int slots = 4;
+  unsigned prefetch_kb = 128;
+  int evict_first = 1;
+  int halves = 1;
+};
+
+const StepTuning& tuning() {
+  static const StepTuning t = [] {
+    StepTuning r;
+    if (const char* v = std::getenv("IPE_STEP_SLOTS")) r.slots = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_PREFETCH_KB")) r.prefetch_kb = static_cast<unsigned>(std::atoi(v));
+    if (const char* v = std::getenv("IPE_STEP_EVICT_FIRST")) r.evict_first = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_HALF")) r.halves = std::atoi(v);
+    return r;
+  }();
+  return t;
+}
+
+size_t fixed_smem(int nt, int slots) {
+  return 1024 + static_cast<size_t>(kConsumers) * slots * kTileBytes + 2 * kMaxStages * 8 + 16 * 4 + 16 +
          static_cast<size_t>(kConsumers) * 32 * 8 * nt * 4;
 }
 
-size_t attn_bytes(int group, int chunks_max) {
+size_t attn_bytes(int group) {
   switch (group) {
-    case 1: return attn_smem_floats<1>(chunks_max) * 4;
-    case 2: return attn_smem_floats<2>(chunks_max) * 4;
-    case 4: return attn_smem_floats<4>(chunks_max) * 4;
-    default: return attn_smem_floats<8>(chunks_max) * 4;
+    case 1: return attn_smem_floats<1>() * 4;
+    case 2: return attn_smem_floats<2>() * 4;
+    case 4: return attn_smem_floats<4>() * 4;
+    default: return attn_smem_floats<8>() * 4;
   }
 }
 
 }  // namespace
 
 size_t decode_step_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity) {
-  const int chunks_max = (capacity + kAttnChunk - 1) / kAttnChunk;
+  (void)capacity;  // attention records are per split, at most kAttnSplitsMax of them
   const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int) + 255) / 256 * 256;
-  return 256 + counters + static_cast<size_t>(batch) * q_heads * chunks_max * kAttnRecord * sizeof(float);
+  return 256 + counters + static_cast<size_t>(batch) * q_heads * kAttnSplitsMax * kAttnRecord * sizeof(float);
 }
 
 cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStream_t stream, const char** message) {
   StepArgs a{};
   a.d = d;
   a.err = err;
-  a.chunks_max = (d.capacity + kAttnChunk - 1) / kAttnChunk;
+  a.max_splits = attn_max_splits(sm_count(), d.batch, d.kv_heads);
   unsigned char* ws = static_cast<unsigned char*>(d.workspace);
   a.grid_bar = reinterpret_cast<unsigned*>(ws);
   a.attn_counters = reinterpret_cast<int*>(ws + 256);
@@ -499,11 +640,19 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   const int group = d.q_heads / d.kv_heads;
   const size_t act = static_cast<size_t>(d.batch) *
                      (std::max(std::max(d.hidden, d.intermediate), d.q_heads * 128) + kPad) * 2;
-  const size_t attn = attn_bytes(group, a.chunks_max);
-  const bool act_smem = fixed_smem(nt) + std::max(act, attn) <= kSmemMax;
-  const size_t smem = fixed_smem(nt) + (act_smem ? std::max(act, attn) : attn);
+  const size_t attn = attn_bytes(group);
+  // Activations stay in shared memory when that leaves room for 4 slots per consumer warp.
+  const bool act_smem = fixed_smem(nt, 4) + std::max(act, attn) <= kSmemMax;
+  const size_t scratch = act_smem ? std::max(act, attn) : attn;
+  int slots = std::min(kMaxSlotsPerWarp, std::max(2, tuning().slots));
+  while (slots > 2 && fixed_smem(nt, slots) + scratch > kSmemMax) --slots;
+  a.slots = slots;
+  a.prefetch_bytes = tuning().prefetch_kb * 1024u;
+  a.evict_first = tuning().evict_first;
+  a.halves = tuning().halves;
+  const size_t smem = fixed_smem(nt, slots) + scratch;
   if (smem > kSmemMax) {
-    *message = "attention scratch for this capacity does not fit in shared memory";
+    *message = "decode-step scratch does not fit in shared memory";
     return cudaErrorInvalidValue;
   }
   // the grid barrier counts arrivals from zero every step

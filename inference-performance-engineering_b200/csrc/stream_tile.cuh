@@ -43,6 +43,28 @@ __device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_
                : "memory");
 }
 
+// The same copy with an L2 eviction-priority policy (from createpolicy) on the source lines.
+__device__ __forceinline__ void bulk_copy_hint(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          dst),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// Asynchronous prefetch of [src, src + bytes) into L2 (16-byte aligned, a multiple of 16 bytes).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// L2 policy that evicts the lines it covers first (data read once).
+__device__ __forceinline__ uint64_t evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
 // acc[h][j] += tile rows (h, g / g+8) x activations xv[c][j] (batch columns 8j..8j+7) over the
 // tile's 128 columns. The MMA's K order is permuted identically for A (weights, 16-byte chunk of
 // 8 consecutive columns per thread) and B (activations, the same 8 columns), so the dot products
@@ -71,25 +93,51 @@ __device__ __forceinline__ void consume_tile(float (&acc)[2][NT][4], uint32_t ba
   }
 }
 
+// The same over one 16-row half of a tile, copied alone (4 KB, [box (2)][row (16)][128 bytes]) to
+// base: columns 0..63 accumulate into acc[0], 64..127 into acc[1] (two independent MMA chains);
+// the caller adds acc[1] into acc[0] when the unit is complete.
+template <int NT>
+__device__ __forceinline__ void consume_half(float (&acc)[2][NT][4], uint32_t base, const uint4 (&xv)[4][NT], int g,
+                                             int t) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int chunk = (c & 1) * 4 + t;
+    uint4 w[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = g + 8 * r;
+      w[r] = lds128(base + (c >> 1) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      mma16816(acc[c >> 1][j], w[0].x, w[1].x, w[0].y, w[1].y, xv[c][j].x, xv[c][j].y);
+      mma16816(acc[c >> 1][j], w[0].z, w[1].z, w[0].w, w[1].w, xv[c][j].z, xv[c][j].w);
+    }
+  }
+}
+
 // Stage B activation rows (row b at src + b * src_stride, K wide) in shared memory xs (row stride
 // xs_stride), RMS-normalised with weight norm_w when it is non-null: bf16(w * bf16(x * rstd)), the
 // reference's two roundings. rstd[b] receives the scale. The nwarps calling warps issue 8
-// independent 16-byte loads per lane before using any, so a row costs one L2 round trip (two when
-// K > 2048 and the row is normalised). to_smem = false computes rstd only. Callers synchronise.
+// independent 16-byte loads per lane (and the norm weight's alongside) before using any, so a row
+// of up to 2048 columns costs one L2 round trip. to_smem = false computes rstd only. Callers
+// synchronise.
 __device__ __forceinline__ void stage_rows(const bf16* src, int64_t src_stride, const bf16* norm_w, float eps, int B,
                                            int K, bf16* xs, int xs_stride, float* rstd, int warp_id, int nwarps,
                                            int lane, bool to_smem) {
   const int chunks = K / 8;
   if (norm_w) {
+    const bool one_round = chunks <= 256;
     for (int b = warp_id; b < B; b += nwarps) {
       const bf16* xr = src + b * src_stride;
-      uint4 v[8];
+      uint4 v[8], wv[8];
       float ss = 0.f;
       for (int base = 0; base < chunks; base += 256) {
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
           const int c = base + u * 32 + lane;
           v[u] = c < chunks ? ldcg16(xr + c * 8) : make_uint4(0, 0, 0, 0);
+          if (one_round && to_smem) wv[u] = c < chunks ? ldg16(norm_w + c * 8) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -104,18 +152,13 @@ __device__ __forceinline__ void stage_rows(const bf16* src, int64_t src_stride, 
       if (lane == 0) rstd[b] = r;
       if (!to_smem) continue;
       for (int base = 0; base < chunks; base += 256) {
-        if (chunks > 256) {  // the row did not fit one round: load this round again
+        if (!one_round) {  // the row did not fit one round: load this round again
 #pragma unroll
           for (int u = 0; u < 8; ++u) {
             const int c = base + u * 32 + lane;
             v[u] = c < chunks ? ldcg16(xr + c * 8) : make_uint4(0, 0, 0, 0);
+            wv[u] = c < chunks ? ldg16(norm_w + c * 8) : make_uint4(0, 0, 0, 0);
           }
-        }
-        uint4 wv[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int c = base + u * 32 + lane;
-          wv[u] = c < chunks ? ldg16(norm_w + c * 8) : make_uint4(0, 0, 0, 0);
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u) {
@@ -161,25 +204,29 @@ struct EpilogueArgs {
 
 // Row block rb's outputs from the complete fp32 sums acc (lane layout of mma m16n8: rows
 // h*16 + g + 8*(e>>1), batch column 8j + 2t + (e&1)). Reads of the residual use L2-only loads.
+// Store / residual also take a single 16-row half: rows rb*32 + 16*first_half + ..., `halves` of
+// them (acc[0] holding the first).
 template <int EPI, int NT>
 __device__ __forceinline__ void row_block_epilogue(const float (&acc)[2][NT][4], int rb, int lane,
-                                                   const EpilogueArgs& a) {
+                                                   const EpilogueArgs& a, int first_half = 0, int halves = 2) {
   const int g = lane >> 2, t = lane & 3, B = a.batch;
   if constexpr (EPI == kGemvStore || EPI == kGemvResidual) {
     bf16* out = static_cast<bf16*>(a.out);
 #pragma unroll
-    for (int h = 0; h < 2; ++h)
+    for (int h = 0; h < 2; ++h) {
+      if (h >= halves) break;
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const int n = rb * 32 + h * 16 + g + 8 * (e >> 1);
+          const int n = rb * 32 + (first_half + h) * 16 + g + 8 * (e >> 1);
           const int b = 8 * j + 2 * t + (e & 1);
           if (b >= B || n >= a.rows) continue;
           bf16* dst = out + b * a.out_stride + n;
           if constexpr (EPI == kGemvStore) *dst = __float2bfloat16_rn(acc[h][j][e]);
           else *dst = __float2bfloat16_rn(ldcg_bf16(dst) + bf16_round(acc[h][j][e]));
         }
+    }
   } else if constexpr (EPI == kGemvSiluMul) {
     bf16* out = static_cast<bf16*>(a.out);
 #pragma unroll

@@ -49,6 +49,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_gemm": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P]),
     "ipe_decode_step": (c_int, [ctypes.c_void_p, _P]),
     "ipe_decode_step_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
+    "ipe_decode_step_grid": (c_int, []),
     "ipe_state_set": (c_int, [_P, c_int, c_int64, _P]),
     "ipe_state_add": (c_int, [_P, c_int, c_int64, _P]),
 }
@@ -71,7 +72,13 @@ class StepDesc(ctypes.Structure):
                 ("cos_table", c_void_p), ("sin_table", c_void_p), ("state", c_void_p), ("tokens", c_void_p),
                 ("x", c_void_p), ("qkv", c_void_p), ("attn", c_void_p), ("act", c_void_p), ("logits", c_void_p),
                 ("partials", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
-                ("history_tokens", c_void_p), ("history_logprobs", c_void_p), ("history_stride", c_int64)]
+                ("history_tokens", c_void_p), ("history_logprobs", c_void_p), ("history_stride", c_int64),
+                ("trace", c_void_p)]
+
+
+def trace_words(layers: int) -> int:
+    """IPE_TRACE_WORDS of include/ipe_b200.h: timestamps per CTA of one traced decode step."""
+    return 25 * layers + 12
 
 
 class NativeUnavailable(RuntimeError):

@@ -245,8 +245,11 @@ def layer_descs(model: PackedModel, k: torch.Tensor, v: torch.Tensor) -> torch.T
     descs = (nat.LayerDesc * len(model.layers))()
     for i, layer in enumerate(model.layers):
         p = layer.ptr
-        descs[i] = nat.LayerDesc(p["in_norm"], p["post_norm"], p["q_norm"], p["k_norm"], p["t_qkv"], p["t_o"],
-                                 p["t_gate_up"], p["t_down"], k[i].data_ptr(), v[i].data_ptr())
+        fields = (p["in_norm"], p["post_norm"], p["q_norm"], p["k_norm"], p["t_qkv"], p["t_o"], p["t_gate_up"],
+                  p["t_down"], k[i].data_ptr(), v[i].data_ptr())
+        if any(f % 16 for f in fields):
+            raise ValueError(f"layer {i}: the decode step needs 16-byte aligned operands")
+        descs[i] = nat.LayerDesc(*fields)
     raw = torch.frombuffer(bytearray(ctypes.string_at(ctypes.addressof(descs), ctypes.sizeof(descs))),
                            dtype=torch.uint8)
     return raw.to(model.device)

@@ -245,15 +245,24 @@ def test_decode_steps_never_synchronize_or_grow_the_allocator(models):
     assert torch.cuda.memory_reserved() == reserved
 
 
-def test_one_kernel_step_agrees_with_the_per_operator_kernels(models, monkeypatch):
+@pytest.mark.parametrize(("name", "batch", "length", "prompt"), [
+    ("small", 2, 20, 6),
+    ("qwen3-1.7b-2layer", 1, 700, 694),   # one row: 11 attention splits merged, half-tile o/down units
+    ("qwen3-1.7b-2layer", 4, 300, 296),   # 4 rows: activations staged in shared memory, 4 splits
+    ("qwen3-1.7b-2layer", 16, 300, 296),  # 16 rows: two MMA column tiles, activations read from L2,
+                                          # one attention split streaming many 32-key sub-chunks
+])
+def test_one_kernel_step_agrees_with_the_per_operator_kernels(models, monkeypatch, name, batch, length, prompt):
     """The graph-replayed one-kernel decode step against the per-operator kernels run eagerly (a
     replaced layer hook selects them): the same math summed in a different order, so within a few
     bf16 ulps of the logits, and the greedy choices agree."""
-    _, gpu = models("small")
-    ids = torch.randint(0, 2048, (2, 20), generator=torch.Generator().manual_seed(12))
-    stepped = teacher_forced(Engine(gpu, batch=2, capacity=24), ids, 6)
+    _, gpu = models(name)
+    vocab = gpu.config.vocab_size
+    ids = torch.randint(0, vocab, (batch, length), generator=torch.Generator().manual_seed(12))
+    stepped = teacher_forced(Engine(gpu, batch=batch, capacity=length + 4), ids, prompt)
+    assert nat.device_error() == 0
     monkeypatch.setattr(engine_module, "decoder_layer", lambda *a, **k: engine_module._BUILTIN_DECODE(*a, **k))
-    per_op = teacher_forced(Engine(gpu, batch=2, capacity=24), ids, 6)
+    per_op = teacher_forced(Engine(gpu, batch=batch, capacity=length + 4), ids, prompt)
     assert ((stepped - per_op).abs() <= 4 * 2 ** -8 * per_op.abs() + 0.05).all()
     assert (stepped.argmax(-1) == per_op.argmax(-1)).float().mean() > 0.9
 
