@@ -100,39 +100,46 @@ def decode_bytes_per_step(config, batch: int, context: float) -> float:
     return weights + batch * kv_token * (context + 1)
 
 
-def time_gate_up_kernel(engine, batch: int, repeats: int = 56) -> dict:
-    """Live CUDA-event timing of the dominant decode kernel (fused RMSNorm + gate/up + SiLU*up
-    GEMV) over the engine's real layer weights, cycling layers so every launch streams from HBM."""
+# DRAM bytes of one decode_step_kernel launch measured by ncu (dram__bytes_read.sum +
+# dram__bytes_write.sum) on the Qwen3-1.7B architecture at batch 1, cache position 514, with 1 and
+# 2 decoder layers: the LM-head part and the per-layer part (captures summarised under profiles/).
+NCU_STEP_FIXED_BYTES = 725.64e6 + 4.65e6 - (102.80e6 + 0.45e6)
+NCU_STEP_LAYER_BYTES = 102.80e6 + 0.45e6
+NCU_STEP_POSITION = 514
+
+
+def step_traffic(config, batch: int, position: int) -> float | None:
+    """The captured traffic scaled to `layers` layers and `position` (K/V rows grow linearly);
+    None where no capture applies (other batch sizes)."""
+    if batch != 1 or config.hidden_size != 2048:
+        return None
+    kv_row = 2 * config.num_key_value_heads * config.head_dim * 2
+    layer = NCU_STEP_LAYER_BYTES + kv_row * (position - NCU_STEP_POSITION)
+    return NCU_STEP_FIXED_BYTES + config.num_hidden_layers * layer
+
+
+def time_step_kernel(engine, batch: int, position: int, repeats: int = 10) -> dict:
+    """Live CUDA-event timing of the dominant kernel, the one-kernel decode step (ipe_decode_step:
+    every layer's weights, the KV cache up to `position` and the LM head in one launch), on the
+    launching stream. The state's position is reset before each launch, so every launch does the
+    same work; each launch streams 3.4 GB of weights, far above L2, so no flush is needed."""
     from ipe_b200 import _native as nat
 
-    c, m = engine.loaded.config, engine._model
     lib = nat.load()
     stream = torch.cuda.current_stream()
-    x = torch.randn((batch, c.hidden_size), device="cuda").bfloat16()
-    out = torch.empty((batch, c.intermediate_size), dtype=torch.bfloat16, device="cuda")
-    layers = m.layers
-
-    ws = engine._buf.linear_workspace
-
-    def launch(i):
-        layer = layers[i % len(layers)]
-        nat.check(lib.ipe_rmsnorm_gate_up_silu(x.data_ptr(), layer.ptr["post_norm"], layer.ptr["t_gate_up"],
-                                               out.data_ptr(), batch, c.hidden_size, c.intermediate_size,
-                                               c.rms_norm_eps, ws.data_ptr(), ws.numel(), stream.cuda_stream),
-                  "gate_up")
-
-    for i in range(len(layers)):
-        launch(i)
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    state = engine._buf.state.data_ptr()
+    events = []
+    for _ in range(repeats + 2):
+        nat.check(lib.ipe_state_set(state, nat.STATE_POS, position, stream.cuda_stream), "ipe_state_set")
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        engine._launch_step(batch, False, stream.cuda_stream)
+        e1.record(stream)
+        events.append((e0, e1))
     torch.cuda.synchronize()
-    start.record(stream)
-    for i in range(repeats):
-        launch(i)
-    end.record(stream)
-    end.synchronize()
-    seconds = start.elapsed_time(end) / 1e3 / repeats
-    algorithmic = 2 * c.intermediate_size * c.hidden_size * 2 + batch * (c.hidden_size + c.intermediate_size) * 2
-    return {"kernel": "stream_gemv_kernel<SiluMul> (ipe_rmsnorm_gate_up_silu)", "seconds": seconds, "bytes": algorithmic}
+    seconds = statistics.mean(a.elapsed_time(b) for a, b in events[2:]) / 1e3
+    return {"kernel": "decode_step_kernel (ipe_decode_step)", "seconds": seconds,
+            "bytes": decode_bytes_per_step(engine.loaded.config, batch, position), "position": position}
 
 
 def run_ours(args, rank: int, world: int) -> dict | None:
@@ -189,7 +196,7 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     assert out.tokens.shape == (batch, new)
     e2e_s = sum(e2e_records)
 
-    kernel = time_gate_up_kernel(engine, batch)
+    kernel = time_step_kernel(engine, batch, prompt + new // 2)
     if world > 1:
         t = torch.tensor([prefill_s, decode_s, total_s, e2e_s, kernel["seconds"]], dtype=torch.float64, device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -221,9 +228,11 @@ def run_ours(args, rank: int, world: int) -> dict | None:
         "decode_hbm": {"bytes_per_step": step_bytes, "achieved_gbs": round(decode_gbs, 1), "peak_gbs": pk["hbm_gbs"],
                        "frac": round(decode_gbs / pk["hbm_gbs"], 4), "peak_source": pk["source"]},
         "roofline": {"kernel": kernel["kernel"], "bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"],
-                     "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "unit": "GB/s", "frac": round(achieved / pk["hbm_gbs"], 4),
+                     "traffic": step_traffic(config, batch, kernel["position"]),
+                     "traffic_source": "ncu dram bytes at 1 and 2 layers, scaled to the layers and position",
                      "bytes_per_launch": kernel["bytes"], "seconds_per_launch": kernel["seconds"],
-                     "peak_source": pk["source"]},
+                     "position": kernel["position"], "peak_source": pk["source"]},
         "e2e": {"value": round(world * batch * new * len(e2e_records) / e2e_s, 2), "unit": "generated tok/s",
                 "definition": "Engine.generate(pinned host prompt) -> host tokens; prefill + decode + copies",
                 "h2d_bytes_per_step": batch * prompt * 8, "d2h_bytes_per_step": batch * new * 12 + batch * 8},
