@@ -74,3 +74,15 @@ def test_a_failed_call_raises_with_the_library_message():
 
 def test_device_error_needs_an_output_pointer():
     assert nat.load().ipe_device_error(0, ctypes.POINTER(ctypes.c_int)()) == 1
+
+
+def test_the_custom_ops_of_the_boundary_are_registered():
+    """torch.ops.ipe_b200 holds the operator set the drop-in boundary names (plus the helpers)."""
+    import torch
+
+    import ipe_b200.ops  # noqa: F401
+
+    for name in ("rms_norm", "rmsnorm_qkv", "qk_norm_rope_append", "decode_attention", "prefill_attention",
+                 "linear_residual", "rmsnorm_gate_up_silu", "lm_head_sample", "gemm", "embed", "sample_logits",
+                 "decode_tiles"):
+        assert hasattr(torch.ops.ipe_b200, name), name
