@@ -213,6 +213,34 @@ int ipe_prefill_attention(const void* q, const void* k_cache, const void* v_cach
 int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epilogue,
              const void* residual, void* stream);
 
+/* ------------------------------------------------------------------ fp32 (plumbing) path
+ * The reference at dtype float32 (TF32 disabled, src/ipe/forward.py:42-43): fp32 storage and fp32
+ * FMA arithmetic, no bf16 rounding points, no tensor cores. Row-major fp32 operands; the RMSNorm
+ * is ipe_rmsnorm with dtype 1 and sampling is ipe_sample_logits. */
+
+/* C[m, n'] = epilogue(A[m, k] . W[n, k]^T) in fp32: store / residual (C = R + acc, R may alias C)
+ * / logits (store); SiLU*up takes W = the gate/up rows interleaved in groups of IPE_GATE_UP_GROUP
+ * (n = 2 * intermediate) and writes n' = n / 2 columns of silu(gate) * up. Replaces the fp32
+ * F.linear calls of src/ipe/forward.py:100-115 and lm_logits (src/ipe/forward.py:145-152). */
+int ipe_gemm_f32(const void* a, const void* w, void* c, int m, int n, int k, int epilogue, const void* residual,
+                 void* stream);
+/* out[i, :] = table[ids[i], :] (fp32); an ID outside [0, vocab) writes zeros and sets device
+ * error 1. Replaces F.embedding (src/ipe/forward.py:125) at fp32. */
+int ipe_embed_f32(const int64_t* ids, int64_t count, const void* table, int64_t vocab, int hidden, void* out,
+                  void* stream);
+/* ipe_qk_norm_rope_append at fp32 (qkv, norm weights, cos/sin tables, q_out and caches fp32; host
+ * start only). Replaces src/ipe/forward.py:101-109 at fp32. */
+int ipe_qk_norm_rope_append_f32(const void* qkv, int batch, int tokens, int q_heads, int kv_heads,
+                                const void* q_norm_weight, const void* k_norm_weight, const void* cos_table,
+                                const void* sin_table, int start, void* q_out, void* k_cache, void* v_cache,
+                                int capacity, float eps, void* stream);
+/* Causal attention in fp32: query t of q [batch, q_heads, tokens, 128] (position start + t) over
+ * cache keys 0 .. start + t, GQA, scale 128^-0.5, fp32 softmax -> out [batch, tokens,
+ * q_heads * 128]. A decode step is tokens = 1, start = its position. Replaces ops.attention
+ * (src/ipe/ops.py:78-101) at fp32. */
+int ipe_attention_f32(const void* q, const void* k_cache, const void* v_cache, void* out, int batch, int q_heads,
+                      int kv_heads, int tokens, int capacity, int start, void* stream);
+
 /* ------------------------------------------------------------------ whole decode step */
 
 /* One decoder layer's operands for ipe_decode_step (device pointers, each 16-byte aligned; the

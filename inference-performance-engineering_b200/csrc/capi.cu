@@ -327,6 +327,63 @@ int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epi
   return cuda_status(e, "ipe_gemm");
 }
 
+// ----------------------------------------------------------------------- fp32 (plumbing) path
+
+int ipe_gemm_f32(const void* a, const void* w, void* c, int m, int n, int k, int epilogue, const void* residual,
+                 void* stream) {
+  if (!a || !w || !c) return fail(IPE_ERR_ARGUMENT, "ipe_gemm_f32: null pointer");
+  if (m < 1 || n < 1 || k < 1) return fail(IPE_ERR_ARGUMENT, "ipe_gemm_f32: m %d n %d k %d", m, n, k);
+  if (epilogue < IPE_EPI_STORE || epilogue > IPE_EPI_LOGITS) return fail(IPE_ERR_ARGUMENT, "ipe_gemm_f32: epilogue");
+  if (epilogue == IPE_EPI_SILU_MUL && n % (2 * IPE_GATE_UP_GROUP))
+    return fail(IPE_ERR_UNSUPPORTED, "ipe_gemm_f32: gate/up rows %d are not whole groups of %d", n, 2 * IPE_GATE_UP_GROUP);
+  if (epilogue == IPE_EPI_RESIDUAL && !residual)
+    return fail(IPE_ERR_ARGUMENT, "ipe_gemm_f32: residual epilogue needs a residual");
+  return cuda_status(ipe::launch_gemm_f32(a, w, c, m, n, k, epilogue, residual, as_stream(stream)), "ipe_gemm_f32");
+}
+
+int ipe_embed_f32(const int64_t* ids, int64_t count, const void* table, int64_t vocab, int hidden, void* out,
+                  void* stream) {
+  if (!ids || !table || !out) return fail(IPE_ERR_ARGUMENT, "ipe_embed_f32: null pointer");
+  if (count < 0 || vocab < 1 || hidden < 1) return fail(IPE_ERR_ARGUMENT, "ipe_embed_f32: bad sizes");
+  if (count == 0) return IPE_OK;
+  ipe::launch_embed_f32(ids, count, table, vocab, hidden, out, device_error_word(), as_stream(stream));
+  return cuda_status(cudaGetLastError(), "ipe_embed_f32");
+}
+
+int ipe_qk_norm_rope_append_f32(const void* qkv, int batch, int tokens, int q_heads, int kv_heads,
+                                const void* q_norm_weight, const void* k_norm_weight, const void* cos_table,
+                                const void* sin_table, int start, void* q_out, void* k_cache, void* v_cache,
+                                int capacity, float eps, void* stream) {
+  if (!qkv || !q_norm_weight || !k_norm_weight || !cos_table || !sin_table || !q_out || !k_cache || !v_cache)
+    return fail(IPE_ERR_ARGUMENT, "ipe_qk_norm_rope_append_f32: null pointer");
+  if (batch < 1 || tokens < 1 || q_heads < 1 || kv_heads < 1 || q_heads % kv_heads || capacity < 1)
+    return fail(IPE_ERR_ARGUMENT, "ipe_qk_norm_rope_append_f32: bad sizes");
+  if (start < 0 || start + tokens > capacity)
+    return fail(IPE_ERR_ARGUMENT, "ipe_qk_norm_rope_append_f32: positions %d..%d outside capacity %d", start,
+                start + tokens - 1, capacity);
+  for (const void* p : {qkv, static_cast<const void*>(q_out), static_cast<const void*>(k_cache),
+                        static_cast<const void*>(v_cache)})
+    if (!aligned16(p)) return fail(IPE_ERR_ARGUMENT, "ipe_qk_norm_rope_append_f32: unaligned operand");
+  ipe::launch_qk_norm_rope_append_f32(qkv, batch, tokens, q_heads, kv_heads, q_norm_weight, k_norm_weight, cos_table,
+                                      sin_table, start, q_out, k_cache, v_cache, capacity, eps, device_error_word(),
+                                      as_stream(stream));
+  return cuda_status(cudaGetLastError(), "ipe_qk_norm_rope_append_f32");
+}
+
+int ipe_attention_f32(const void* q, const void* k_cache, const void* v_cache, void* out, int batch, int q_heads,
+                      int kv_heads, int tokens, int capacity, int start, void* stream) {
+  if (!q || !k_cache || !v_cache || !out) return fail(IPE_ERR_ARGUMENT, "ipe_attention_f32: null pointer");
+  if (batch < 1 || tokens < 1 || q_heads < 1 || kv_heads < 1 || q_heads % kv_heads || capacity < 1)
+    return fail(IPE_ERR_ARGUMENT, "ipe_attention_f32: bad sizes");
+  if (start < 0 || start + tokens > capacity)
+    return fail(IPE_ERR_ARGUMENT, "ipe_attention_f32: positions %d..%d outside capacity %d", start, start + tokens - 1,
+                capacity);
+  if (!aligned16(k_cache) || !aligned16(v_cache)) return fail(IPE_ERR_ARGUMENT, "ipe_attention_f32: unaligned cache");
+  return cuda_status(ipe::launch_attention_f32(q, k_cache, v_cache, out, batch, q_heads, kv_heads, tokens, capacity,
+                                               start, as_stream(stream)),
+                     "ipe_attention_f32");
+}
+
 size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capacity) {
   if (batch < 1 || q_heads < 1 || kv_heads < 1 || capacity < 1) return 0;
   return ipe::decode_step_workspace_bytes(batch, q_heads, kv_heads, capacity);

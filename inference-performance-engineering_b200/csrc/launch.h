@@ -77,4 +77,16 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
 cudaError_t launch_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epilogue,
                         const void* residual, int* err, cudaStream_t stream, const char** message);
 
+// fp32 (plumbing) path, fp32.cu
+cudaError_t launch_gemm_f32(const void* a, const void* w, void* c, int m, int n, int k, int epilogue,
+                            const void* residual, cudaStream_t stream);
+void launch_embed_f32(const int64_t* ids, int64_t count, const void* table, int64_t vocab, int hidden, void* out,
+                      int* err, cudaStream_t stream);
+void launch_qk_norm_rope_append_f32(const void* qkv, int batch, int tokens, int q_heads, int kv_heads, const void* qn,
+                                    const void* kn, const void* cos_t, const void* sin_t, int start, void* q_out,
+                                    void* k_cache, void* v_cache, int capacity, float eps, int* err,
+                                    cudaStream_t stream);
+cudaError_t launch_attention_f32(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
+                                 int kv_heads, int tokens, int capacity, int start, cudaStream_t stream);
+
 }  // namespace ipe

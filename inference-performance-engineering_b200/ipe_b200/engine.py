@@ -24,6 +24,7 @@ from dataclasses import dataclass
 import torch
 
 from ipe_b200 import _native as nat
+from ipe_b200 import fp32 as _fp32
 from ipe_b200 import model as _model
 from ipe_b200 import ops
 from ipe_b200.forward import INTEGER_DTYPES, check_backend, check_dtype, check_token_ids
@@ -59,6 +60,14 @@ def sample(logits: torch.Tensor, temperature: float,
     return ops.sample_logits(logits.contiguous(), float(temperature), int(seed.item()))
 
 
+def _step_seed(seed: int, step: int) -> int:
+    """A 64-bit seed per generation step for the fp32 path's sampler (splitmix64 finaliser)."""
+    z = (seed + 0x9E3779B97F4A7C15 * (step + 1)) & (2**64 - 1)
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & (2**64 - 1)
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & (2**64 - 1)
+    return z ^ (z >> 31)
+
+
 def _float_bits(value: float) -> int:
     return struct.unpack("<i", struct.pack("<f", float(value)))[0]
 
@@ -79,6 +88,18 @@ class Engine:
         if type(capacity) is not int or not 1 <= capacity <= config.max_position_embeddings:
             raise ValueError(f"capacity {capacity!r}: expected an integer from 1 to {config.max_position_embeddings}")
         self.loaded, self.dtype, self.backend, self.capacity = loaded, dtype, backend, capacity
+        self.batch = 0
+        self.length = 0
+        self._f32 = None
+        if dtype == torch.float32:
+            # the fp32 path: reference-precision kernels, one launch per operator (ipe_b200.fp32)
+            self._f32 = _fp32.fp32_model(loaded)
+            shape = (config.num_hidden_layers, batch, config.num_key_value_heads, capacity, config.head_dim)
+            self._k = torch.full(shape, float("nan"), dtype=dtype, device=self._f32.device)
+            self._v = torch.full(shape, float("nan"), dtype=dtype, device=self._f32.device)
+            self._cos, self._sin = self._f32.decode_rotary(capacity)
+            self._f32_buffers: dict[tuple[int, int], _fp32.Fp32Buffers] = {}
+            return
         self._model = _model.packed_model(loaded)
         device = self._model.device
         shape = (config.num_hidden_layers, batch, config.num_key_value_heads, capacity, config.head_dim)
@@ -92,8 +113,6 @@ class Engine:
         self._graphs: dict[tuple[int, bool], torch.cuda.CUDAGraph] = {}
         self._warm: set[tuple[int, bool]] = set()  # step variants already run once outside capture
         self._device_pos = 0  # what state[POS] holds once the queued work has run
-        self.batch = 0
-        self.length = 0
 
     # ------------------------------------------------------------------------------- public API
 
@@ -103,7 +122,7 @@ class Engine:
         if batch > self._k.shape[1]:
             raise ValueError(f"token_ids: batch {batch} exceeds the {self._k.shape[1]} allocated rows")
         self.batch = self.length = 0
-        cos, sin = self._model.prefill_rotary(length)
+        cos, sin = (self._f32 or self._model).prefill_rotary(length)
         logits = self._step(token_ids, (cos, sin), 0)
         self.batch, self.length = batch, length
         return logits.clone()
@@ -139,8 +158,9 @@ class Engine:
         _, length = check_token_ids(self.loaded.config, token_ids, self.capacity)
         if length + max_new_tokens - 1 > self.capacity:
             raise ValueError(f"prompt length {length} + max_new_tokens {max_new_tokens} - 1 exceeds capacity {self.capacity}")
-        tokens, logprobs, lengths, produced = self._generate_on_device(token_ids, max_new_tokens, float(temperature),
-                                                                       int(seed), tuple(stop_ids))
+        run = self._generate_f32 if self._f32 is not None else self._generate_on_device
+        tokens, logprobs, lengths, produced = run(token_ids, max_new_tokens, float(temperature), int(seed),
+                                                  tuple(stop_ids))
         return Generation(tokens[:, :produced].cpu(), logprobs[:, :produced].cpu(), lengths.cpu())
 
     def _generate_on_device(self, token_ids, max_new_tokens: int, temperature: float, seed: int,
@@ -185,6 +205,32 @@ class Engine:
             nat.check(lib.ipe_state_set(state, nat.STATE_TEMPERATURE, 0, stream), "ipe_state_set")
         return tokens[:, :max_new_tokens].clone(), logprobs[:, :max_new_tokens].clone(), lengths, produced
 
+    def _generate_f32(self, token_ids, max_new_tokens: int, temperature: float, seed: int,
+                      stop_ids: tuple[int, ...] = ()):
+        """The fp32 generation loop: prefill, then per token the library sampler on the step's fp32
+        logits (Gumbel draws keyed by a per-step seed) and a decode step on the sampled IDs."""
+        logits = self.prefill(token_ids)
+        device, batch = self._f32.device, self.batch
+        tokens = torch.empty((batch, max_new_tokens), dtype=torch.int64, device=device)
+        logprobs = torch.empty((batch, max_new_tokens), dtype=torch.float32, device=device)
+        stops = torch.tensor(stop_ids, dtype=torch.int64, device=device) if stop_ids else None
+        lengths = torch.full((batch,), max_new_tokens, dtype=torch.int64, device=device)
+        stopped = torch.zeros(batch, dtype=torch.bool, device=device)
+        produced = max_new_tokens
+        for step in range(max_new_tokens):
+            token, logprob = ops.sample_logits(logits, temperature, _step_seed(seed, step))
+            tokens[:, step], logprobs[:, step] = token, logprob
+            if stops is not None:
+                first = torch.isin(token, stops) & ~stopped
+                lengths = torch.where(first, step + 1, lengths)
+                stopped |= first
+                if bool(stopped.all()):
+                    produced = step + 1
+                    break
+            if step + 1 < max_new_tokens:
+                logits = self.decode(token)
+        return tokens, logprobs, lengths, produced
+
     def kernel_launches(self, prompt: int, new_tokens: int) -> dict[str, int]:
         """How many library kernels one `generate(prompt, new_tokens)` launches, by phase."""
         layers = self.loaded.config.num_hidden_layers
@@ -205,6 +251,8 @@ class Engine:
     def _step(self, token_ids: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor], start: int) -> torch.Tensor:
         """Run all layers for token_ids [B, T] at positions start..start+T-1 and the LM head on the
         last position; fp32 logits [B, V] in the engine's logits buffer (src/ipe/engine.py:103-111)."""
+        if self._f32 is not None:
+            return self._step_f32(token_ids, start)
         if start == 0:
             return self._prefill(token_ids, rope)
         if token_ids.shape[1] != 1:
@@ -213,6 +261,21 @@ class Engine:
         self._buf.tokens[:b].copy_(token_ids[:, 0], non_blocking=True)
         self._run_decode(start, batch=b)
         return self._buf.logits[:b]
+
+    def _step_f32(self, token_ids: torch.Tensor, start: int) -> torch.Tensor:
+        """The fp32 path of _step: token_ids [B, T] at positions start.., logits of each row's last
+        position."""
+        batch, tokens = token_ids.shape
+        buf = self._f32_buffers.get((batch, tokens))
+        if buf is None:
+            if len(self._f32_buffers) > 8:
+                self._f32_buffers.clear()
+            buf = self._f32_buffers[(batch, tokens)] = _fp32.Fp32Buffers(self._f32, batch, tokens)
+        buf.ids.copy_(token_ids.reshape(-1), non_blocking=True)
+        cos, sin = self._f32.prefill_rotary(tokens) if start == 0 else (self._cos, self._sin)
+        stream = torch.cuda.current_stream().cuda_stream
+        _fp32.run_layers(self._f32, buf, self._k, self._v, start, self.capacity, cos, sin, stream)
+        return _fp32.step_logits(self._f32, buf, stream)
 
     def _prefill(self, token_ids: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
         c, m = self.loaded.config, self._model

@@ -7,8 +7,10 @@ Drop-in for the reference's `ipe.forward` (src/ipe/forward.py):
   prompt (`:155-170`);
 - `final_hidden` / `lm_logits`: the final-normed states and the tied LM head (`:133-152`).
 
-The CUDA path computes in bf16. fp64 (the reference's oracle) and fp32 are rejected with a
-ValueError: the fp64 oracle is a CPU program and is not part of this package.
+The CUDA path computes in bf16 (weight-streaming and tcgen05 kernels) or in fp32 (the
+reference-precision kernels of ipe_b200.fp32, for the plumbing configuration). fp64 (the
+reference's oracle) is rejected with a ValueError: the fp64 oracle is a CPU program and is not part
+of this package.
 """
 
 from __future__ import annotations
@@ -19,12 +21,13 @@ import torch
 
 from ipe_b200.config import check_supported
 from ipe_b200.model import PackedModel, PrefillBuffers, packed_model, run_prefill_layers
+from ipe_b200 import fp32 as _fp32
 from ipe_b200 import ops
 from ipe_b200 import _native as nat
 
 INTEGER_DTYPES = (torch.int64, torch.int32, torch.int16, torch.int8, torch.uint8)
 BACKENDS = ("math", "sdpa")
-RUN_DTYPES = (torch.bfloat16,)
+RUN_DTYPES = (torch.bfloat16, torch.float32)
 
 
 def check_dtype(loaded, dtype: torch.dtype, allowed: Sequence[torch.dtype]) -> None:
@@ -37,11 +40,11 @@ def check_dtype(loaded, dtype: torch.dtype, allowed: Sequence[torch.dtype]) -> N
     if stored.device.type == "cuda" and dtype == torch.float32 and torch.backends.cuda.matmul.fp32_precision == "tf32":
         raise ValueError("dtype float32 on cuda: TF32 matmul is enabled; set torch.backends.cuda.matmul.fp32_precision = 'ieee'")
     if dtype not in RUN_DTYPES:
-        raise ValueError(f"dtype {dtype!r}: the CUDA path computes in bfloat16 only")
+        raise ValueError(f"dtype {dtype!r}: the CUDA path computes in bfloat16 or float32")
     if stored.device.type != "cuda":
         raise ValueError(f"device {stored.device}: the CUDA path needs the weights on a CUDA device")
-    if stored.dtype != torch.bfloat16:
-        raise ValueError(f"weights stored as {stored.dtype}: the CUDA path streams bfloat16 weights")
+    if dtype == torch.bfloat16 and stored.dtype != torch.bfloat16:
+        raise ValueError(f"weights stored as {stored.dtype}: the bfloat16 path streams bfloat16 weights")
     check_supported(loaded.config)
 
 
@@ -106,6 +109,8 @@ def final_hidden(loaded, token_ids: torch.Tensor, *, dtype: torch.dtype, backend
     check_dtype(loaded, dtype, (torch.bfloat16, torch.float32, torch.float64))
     check_backend(backend)
     batch, length = check_token_ids(loaded.config, token_ids, loaded.config.max_position_embeddings)
+    if dtype == torch.float32:
+        return _fp32.uncached_hidden(_fp32.fp32_model(loaded), token_ids).view(batch, length, -1)
     return _uncached_hidden(packed_model(loaded), token_ids).view(batch, length, -1)
 
 
@@ -116,10 +121,12 @@ def lm_logits(loaded, hidden: torch.Tensor) -> torch.Tensor:
     if hidden.device != loaded.weights.lm_head.device:
         raise ValueError(f"hidden: on {hidden.device}, weights on {loaded.weights.lm_head.device}")
     check_dtype(loaded, hidden.dtype, (torch.bfloat16, torch.float32, torch.float64))
-    model = packed_model(loaded)
     rows = hidden.reshape(-1, hidden.shape[-1]).contiguous()
     logits = torch.empty((rows.shape[0], loaded.config.vocab_size), dtype=torch.float32, device=hidden.device)
-    ops.gemm(rows, model.embed, logits, nat.EPI_LOGITS)
+    if hidden.dtype == torch.float32:
+        _fp32.lm_logits(_fp32.fp32_model(loaded), rows, logits, torch.cuda.current_stream().cuda_stream)
+        return logits.view(*hidden.shape[:-1], -1)
+    ops.gemm(rows, packed_model(loaded).embed, logits, nat.EPI_LOGITS)
     return logits.to(hidden.dtype).view(*hidden.shape[:-1], -1)
 
 
@@ -131,6 +138,15 @@ def forward_full(loaded, token_ids: torch.Tensor, *, dtype: torch.dtype,
     check_backend(backend)
     batch, length = check_token_ids(loaded.config, token_ids, loaded.config.max_position_embeddings)
     rows = None if logit_positions is None else _check_logit_positions(logit_positions, length)
+    if dtype == torch.float32:
+        model32 = _fp32.fp32_model(loaded)
+        hidden = _fp32.uncached_hidden(model32, token_ids).view(batch, length, -1)
+        if rows is not None:
+            hidden = hidden[:, rows.to(hidden.device)]
+        selected = hidden.reshape(-1, hidden.shape[-1]).contiguous()
+        logits = torch.empty((selected.shape[0], loaded.config.vocab_size), dtype=torch.float32, device=model32.device)
+        _fp32.lm_logits(model32, selected, logits, torch.cuda.current_stream().cuda_stream)
+        return logits.view(batch, -1, loaded.config.vocab_size)
     model = packed_model(loaded)
     hidden = _uncached_hidden(model, token_ids).view(batch, length, -1)
     if rows is not None:
