@@ -34,6 +34,8 @@ typedef enum {
   IPE_EPI_SILU_MUL = 2, /* B rows interleaved in groups of 64 (gate, up); C[m,n/2] =
                            bf16(bf16(silu(bf16(gate))) * bf16(up))                  */
   IPE_EPI_LOGITS = 3,   /* C (fp32)[m,n] = float(bf16(acc))                          */
+  IPE_EPI_PARTIAL = 4,  /* C (fp32)[m,n] = acc, unrounded: a tensor-parallel rank's part
+                           of a sum that ipe_add_partial completes after the all-reduce */
 } ipe_epilogue;
 
 /* Device-resident step state: int64_t[IPE_STATE_WORDS]. Kernels given a non-null state read the
@@ -124,6 +126,16 @@ int ipe_rmsnorm_gate_up_silu(const void* x, const void* norm_weight, const void*
                              void* act_out, int batch, int hidden, int intermediate, float eps,
                              void* workspace, size_t workspace_bytes, void* stream);
 
+/* Tensor-parallel pieces (one rank of t holding a column shard of a row-parallel layer):
+ * out (fp32) [b, n] = a[b, :] . w[n, :], unrounded, to be summed over the ranks (an all-reduce)
+ * and then applied by ipe_add_partial. Replaces the rank's share of the o_proj / down_proj
+ * products of src/ipe/forward.py:113, :115 under a Megatron split. */
+int ipe_linear_partial(const void* a, const void* w, float* out, int batch, int in_features, int out_features,
+                       void* workspace, size_t workspace_bytes, void* stream);
+/* x[i] = bf16(x[i] + bf16(sum[i])) for i < count: the residual add of a layer whose product was
+ * summed in fp32 over the ranks, rounded once as the unsplit layer rounds. */
+int ipe_add_partial(void* x, const float* sum, int64_t count, void* stream);
+
 /* Final RMSNorm of x rows (row b at x + b*x_row_stride elements), tied LM head (its decode
  * tiles), fp32 logits
  * (bf16-rounded then widened, as the reference), and per-block sampling partials
@@ -134,6 +146,13 @@ int ipe_lm_head(const void* x, int64_t x_row_stride, const void* norm_weight, co
                 float* logits, float* partials, int batch, int hidden, int vocab, float eps,
                 float temperature, uint64_t seed, const int64_t* state, void* stream);
 int ipe_lm_head_parts(int vocab);
+/* ipe_lm_head over a vocabulary shard: embed_tiles holds rows vocab_offset .. vocab_offset +
+ * vocab_rows - 1 (vocab_offset a multiple of 32), logits is [batch, vocab_rows], and the records
+ * carry global vocabulary IDs and Gumbel draws, so ranks' records gathered in order sample as the
+ * unsharded head would (ipe_sample_records). */
+int ipe_lm_head_shard(const void* x, int64_t x_row_stride, const void* norm_weight, const void* embed_tiles,
+                      float* logits, float* partials, int batch, int hidden, int vocab_rows, int vocab_offset,
+                      float eps, float temperature, uint64_t seed, const int64_t* state, void* stream);
 
 /* Token and untempered log-probability per row from the partials: argmax (lowest ID on ties)
  * when temperature == 0, else Gumbel-max. Writes tokens[b*stride + step] and logprobs[...] with
@@ -142,6 +161,12 @@ int ipe_lm_head_parts(int vocab);
 int ipe_sample(const float* partials, const float* logits, int batch, int vocab, float temperature,
                int64_t* state, int64_t* tokens, float* logprobs, int64_t stride,
                int64_t* next_tokens, void* stream);
+
+/* ipe_sample from `parts` records alone (no logits): the chosen token's logit comes from the
+ * records (the maximum for argmax, the carried logit for the Gumbel winner). For records gathered
+ * from vocabulary shards; padding records (max -inf, sum 0) are neutral. */
+int ipe_sample_records(const float* partials, int parts, int batch, float temperature, int64_t* state,
+                       int64_t* tokens, float* logprobs, int64_t stride, int64_t* next_tokens, void* stream);
 
 /* The same rule over a logits matrix [rows, vocab] (fp32) already in memory, any number of rows:
  * tokens[r], logprobs[r]. Gumbel noise is drawn from (seed, row, vocab id). Replaces

@@ -190,6 +190,24 @@ int ipe_linear_residual(const void* act, const void* w, void* x, int batch, int 
   return run_gemv("ipe_linear_residual", a, workspace, workspace_bytes, as_stream(stream));
 }
 
+int ipe_linear_partial(const void* act, const void* w, float* out, int batch, int in_features, int out_features,
+                       void* workspace, size_t workspace_bytes, void* stream) {
+  int s = gemv_checks("ipe_linear_partial", act, w, out, batch, in_features, out_features);
+  if (s) return s;
+  ipe::GemvArgs a{};
+  a.x = act; a.x_stride = in_features; a.w = w; a.rows = out_features; a.k = in_features; a.batch = batch;
+  a.out = out; a.out_stride = out_features; a.epilogue = ipe::kGemvPartial;
+  return run_gemv("ipe_linear_partial", a, workspace, workspace_bytes, as_stream(stream));
+}
+
+int ipe_add_partial(void* x, const float* sum, int64_t count, void* stream) {
+  if (!x || !sum) return fail(IPE_ERR_ARGUMENT, "ipe_add_partial: null pointer");
+  if (count < 0) return fail(IPE_ERR_ARGUMENT, "ipe_add_partial: count %lld", static_cast<long long>(count));
+  if (count == 0) return IPE_OK;
+  ipe::launch_add_partial(x, sum, count, as_stream(stream));
+  return cuda_status(cudaGetLastError(), "ipe_add_partial");
+}
+
 int ipe_rmsnorm_gate_up_silu(const void* x, const void* norm_weight, const void* w_gate_up, void* act_out, int batch,
                              int hidden, int intermediate, float eps, void* workspace, size_t workspace_bytes,
                              void* stream) {
@@ -222,6 +240,24 @@ int ipe_lm_head(const void* x, int64_t x_row_stride, const void* norm_weight, co
   return run_gemv("ipe_lm_head", a, nullptr, 0, as_stream(stream));
 }
 
+int ipe_lm_head_shard(const void* x, int64_t x_row_stride, const void* norm_weight, const void* embed_tiles,
+                      float* logits, float* partials, int batch, int hidden, int vocab_rows, int vocab_offset,
+                      float eps, float temperature, uint64_t seed, const int64_t* state, void* stream) {
+  int s = gemv_checks("ipe_lm_head_shard", x, embed_tiles, logits, batch, hidden, vocab_rows);
+  if (s) return s;
+  if (!partials || !norm_weight || !aligned16(norm_weight))
+    return fail(IPE_ERR_ARGUMENT, "ipe_lm_head_shard: null pointer");
+  if (vocab_offset < 0 || vocab_offset % 32) return fail(IPE_ERR_ARGUMENT, "ipe_lm_head_shard: vocab_offset %d", vocab_offset);
+  if (x_row_stride < hidden || x_row_stride % 8) return fail(IPE_ERR_ARGUMENT, "ipe_lm_head_shard: x_row_stride");
+  if (!(temperature >= 0.f)) return fail(IPE_ERR_ARGUMENT, "ipe_lm_head_shard: temperature must be >= 0");
+  ipe::GemvArgs a{};
+  a.x = x; a.x_stride = x_row_stride; a.norm_weight = norm_weight; a.eps = eps; a.w = embed_tiles; a.rows = vocab_rows;
+  a.k = hidden; a.batch = batch; a.out = logits; a.out_stride = vocab_rows; a.partials = partials;
+  a.temperature = temperature; a.seed = seed; a.state = state; a.epilogue = ipe::kGemvLogits;
+  a.row_offset = vocab_offset;
+  return run_gemv("ipe_lm_head_shard", a, nullptr, 0, as_stream(stream));
+}
+
 int ipe_sample(const float* partials, const float* logits, int batch, int vocab, float temperature, int64_t* state,
                int64_t* tokens, float* logprobs, int64_t stride, int64_t* next_tokens, void* stream) {
   if (!partials || !logits || !tokens || !logprobs) return fail(IPE_ERR_ARGUMENT, "ipe_sample: null pointer");
@@ -230,6 +266,16 @@ int ipe_sample(const float* partials, const float* logits, int batch, int vocab,
   ipe::launch_sample(partials, ipe_lm_head_parts(vocab), logits, batch, vocab, temperature, state, tokens, logprobs,
                      stride, next_tokens, as_stream(stream));
   return cuda_status(cudaGetLastError(), "ipe_sample");
+}
+
+int ipe_sample_records(const float* partials, int parts, int batch, float temperature, int64_t* state,
+                       int64_t* tokens, float* logprobs, int64_t stride, int64_t* next_tokens, void* stream) {
+  if (!partials || !tokens || !logprobs) return fail(IPE_ERR_ARGUMENT, "ipe_sample_records: null pointer");
+  if (parts < 1 || batch < 1 || batch > 16 || stride < 1) return fail(IPE_ERR_ARGUMENT, "ipe_sample_records: bad sizes");
+  if (!(temperature >= 0.f)) return fail(IPE_ERR_ARGUMENT, "ipe_sample_records: temperature must be >= 0");
+  ipe::launch_sample(partials, parts, nullptr, batch, 0, temperature, state, tokens, logprobs, stride, next_tokens,
+                     as_stream(stream));
+  return cuda_status(cudaGetLastError(), "ipe_sample_records");
 }
 
 int ipe_sample_logits(const float* logits, int64_t rows, int vocab, float temperature, uint64_t seed,
@@ -316,7 +362,7 @@ int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epi
   if (!a || !b || !c) return fail(IPE_ERR_ARGUMENT, "ipe_gemm: null pointer");
   if (m < 1 || n < 1 || k < 1) return fail(IPE_ERR_ARGUMENT, "ipe_gemm: m %d n %d k %d", m, n, k);
   if (n % 128 || k % 64) return fail(IPE_ERR_UNSUPPORTED, "ipe_gemm: n %% 128 and k %% 64 must be 0 (n %d k %d)", n, k);
-  if (epilogue < IPE_EPI_STORE || epilogue > IPE_EPI_LOGITS) return fail(IPE_ERR_ARGUMENT, "ipe_gemm: epilogue");
+  if (epilogue < IPE_EPI_STORE || epilogue > IPE_EPI_PARTIAL) return fail(IPE_ERR_ARGUMENT, "ipe_gemm: epilogue");
   if (epilogue == IPE_EPI_RESIDUAL && (!residual || !aligned16(residual)))
     return fail(IPE_ERR_ARGUMENT, "ipe_gemm: residual epilogue needs an aligned residual");
   if (!aligned16(a) || !aligned16(b) || !aligned16(c)) return fail(IPE_ERR_ARGUMENT, "ipe_gemm: unaligned operand");

@@ -516,19 +516,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     const float temperature = __int_as_float(static_cast<int>(state[IPE_STATE_TEMPERATURE]));
     const int64_t step = state[IPE_STATE_STEP];
     for (int b = cw; b < B; b += kConsumers) {
-      Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
-      for (int p = lane; p < parts; p += 32) {
-        const float* rec = d.partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS;
-        st = merge(st, Stat{__ldcg(rec), __ldcg(rec + 1), __float_as_int(__ldcg(rec + 4)), __ldcg(rec + 2),
-                            __float_as_int(__ldcg(rec + 5))});
-      }
+      Stat st = empty_stat();
+      for (int p = lane; p < parts; p += 32)
+        st = merge(st, load_stat(d.partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
-               __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
-               __shfl_xor_sync(0xffffffffu, st.garg, o)};
-        st = merge(st, y);
-      }
+      for (int o = 16; o > 0; o >>= 1) st = merge(st, shfl_xor_stat(st, o));
       if (lane == 0) {
         const int token = temperature > 0.f ? st.garg : st.arg;
         const float logit = __ldcg(d.logits + static_cast<int64_t>(b) * d.vocab + token);

@@ -159,4 +159,18 @@ void launch_state_update(int64_t* state, int index, int64_t value, bool add, cud
   state_update_kernel<<<1, 1, 0, stream>>>(state, index, value, add ? 1 : 0);
 }
 
+// ------------------------------------------------------------------ residual add of a summed part
+// x = bf16(x + bf16(sum)): the residual update of a layer whose product was summed in fp32 over
+// tensor-parallel ranks, with the rounding points of the unsplit layer.
+__global__ void __launch_bounds__(256) add_partial_kernel(bf16* __restrict__ x, const float* __restrict__ sum,
+                                                          int64_t count) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < count) x[i] = __float2bfloat16_rn(__bfloat162float(x[i]) + bf16_round(sum[i]));
+}
+
+void launch_add_partial(void* x, const float* sum, int64_t count, cudaStream_t stream) {
+  add_partial_kernel<<<static_cast<unsigned>((count + 255) / 256), 256, 0, stream>>>(static_cast<bf16*>(x), sum,
+                                                                                      count);
+}
+
 }  // namespace ipe

@@ -246,6 +246,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
               *reinterpret_cast<float4*>(out + 4 * q) =
                   make_float4(bf16_round(v[4 * q]), bf16_round(v[4 * q + 1]), bf16_round(v[4 * q + 2]),
                               bf16_round(v[4 * q + 3]));
+          } else if constexpr (EPI == IPE_EPI_PARTIAL) {  // unrounded fp32 sums
+            float* out = static_cast<float*>(c) + static_cast<int64_t>(row) * N + col;
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              *reinterpret_cast<float4*>(out + 4 * q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
           } else {
             bf16* out = static_cast<bf16*>(c) + static_cast<int64_t>(row) * N + col;
 #pragma unroll
@@ -311,6 +316,7 @@ cudaError_t run_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, void*
     case IPE_EPI_STORE: return run<BN, IPE_EPI_STORE>(ma, mb, c, residual, m, n, k, err, stream);
     case IPE_EPI_RESIDUAL: return run<BN, IPE_EPI_RESIDUAL>(ma, mb, c, residual, m, n, k, err, stream);
     case IPE_EPI_SILU_MUL: return run<BN, IPE_EPI_SILU_MUL>(ma, mb, c, residual, m, n, k, err, stream);
+    case IPE_EPI_PARTIAL: return run<BN, IPE_EPI_PARTIAL>(ma, mb, c, residual, m, n, k, err, stream);
     default: return run<BN, IPE_EPI_LOGITS>(ma, mb, c, residual, m, n, k, err, stream);
   }
 }

@@ -250,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const GemvArgs
     }
 
     // ---------------------------------------------------------------- epilogue
-    EpilogueArgs ea{a.out, a.out_stride, a.rows, B, a.partials, a.state, a.temperature, a.seed};
+    EpilogueArgs ea{a.out, a.out_stride, a.rows, B, a.partials, a.state, a.temperature, a.seed, a.row_offset};
     row_block_epilogue<EPI, NT>(acc, rb, lane, ea);
   }
 }
@@ -303,6 +303,7 @@ cudaError_t dispatch(const GemvArgs& a, const Plan& plan, cudaStream_t stream) {
     case kGemvStore: return launch_one<NT, kGemvStore, true, ACT>(a, plan, stream);
     case kGemvResidual: return launch_one<NT, kGemvResidual, false, ACT>(a, plan, stream);
     case kGemvSiluMul: return launch_one<NT, kGemvSiluMul, true, ACT>(a, plan, stream);
+    case kGemvPartial: return launch_one<NT, kGemvPartial, false, ACT>(a, plan, stream);
     default: return launch_one<NT, kGemvLogits, true, ACT>(a, plan, stream);
   }
 }

@@ -21,7 +21,7 @@ void launch_qk_norm_rope_append(const void* qkv, int batch, int tokens, int q_he
 void launch_state_update(int64_t* state, int index, int64_t value, bool add, cudaStream_t stream);
 
 // Decode weight-streaming linear layers (gemv.cu).
-enum GemvEpilogue : int { kGemvStore = 0, kGemvResidual = 1, kGemvSiluMul = 2, kGemvLogits = 3 };
+enum GemvEpilogue : int { kGemvStore = 0, kGemvResidual = 1, kGemvSiluMul = 2, kGemvLogits = 3, kGemvPartial = 4 };
 struct GemvArgs {
   const void* x;           // bf16 activations, row b at x + b * x_stride
   int64_t x_stride;
@@ -41,6 +41,7 @@ struct GemvArgs {
   int* err;
   float* slots;    // split-K partial tiles (set by launch_gemv from the workspace)
   int* counters;   // split-K arrival counters, zero between launches
+  int row_offset;  // logits: global vocabulary ID of weight row 0 (a vocabulary shard)
 };
 // Bytes of the decode tile layout of a [rows, k] matrix (pair: two [rows, k] gate/up matrices).
 size_t decode_tiles_bytes(int rows, int k, bool pair);
@@ -88,5 +89,7 @@ void launch_qk_norm_rope_append_f32(const void* qkv, int batch, int tokens, int 
                                     cudaStream_t stream);
 cudaError_t launch_attention_f32(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                  int kv_heads, int tokens, int capacity, int start, cudaStream_t stream);
+
+void launch_add_partial(void* x, const float* sum, int64_t count, cudaStream_t stream);
 
 }  // namespace ipe

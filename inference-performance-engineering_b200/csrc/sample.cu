@@ -17,20 +17,13 @@ __global__ void __launch_bounds__(1024) sample_kernel(const float* __restrict__ 
   const int b = warp / per_row, sub = warp % per_row;
   const int64_t step = state ? state[IPE_STATE_STEP] : 0;
   const float temperature = state ? __int_as_float(static_cast<int>(state[IPE_STATE_TEMPERATURE])) : temperature_arg;
-  Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
+  Stat st = empty_stat();
   if (b < B) {
-    for (int p = sub * 32 + lane; p < parts; p += per_row * 32) {
-      const float* rec = partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS;
-      st = merge(st, Stat{rec[0], rec[1], __float_as_int(rec[4]), rec[2], __float_as_int(rec[5])});
-    }
+    for (int p = sub * 32 + lane; p < parts; p += per_row * 32)
+      st = merge(st, load_stat(partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
-           __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
-           __shfl_xor_sync(0xffffffffu, st.garg, o)};
-    st = merge(st, y);
-  }
+  for (int o = 16; o > 0; o >>= 1) st = merge(st, shfl_xor_stat(st, o));
   if (lane == 0) shared[warp] = st;
   __syncthreads();
   if (threadIdx.x < B) {
@@ -38,7 +31,9 @@ __global__ void __launch_bounds__(1024) sample_kernel(const float* __restrict__ 
     Stat r = shared[row * per_row];
     for (int i = 1; i < per_row; ++i) r = merge(r, shared[row * per_row + i]);
     const int token = temperature > 0.f ? r.garg : r.arg;
-    const float logit = logits[static_cast<int64_t>(row) * V + token];
+    // the chosen token's logit: from the logits when given, else from the records (the argmax's is
+    // the maximum, the Gumbel winner's is carried with it)
+    const float logit = logits ? logits[static_cast<int64_t>(row) * V + token] : (temperature > 0.f ? r.gl : r.m);
     const float lp = (logit - r.m) - logf(r.s);
     tokens[row * stride + step] = token;
     logprobs[row * stride + step] = lp;
@@ -55,10 +50,10 @@ __global__ void __launch_bounds__(256) sample_logits_kernel(const float* __restr
                                                             int64_t stride) {
   const int64_t row = blockIdx.x;
   const float* l = logits + row * V;
-  Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
+  Stat st = empty_stat();
   for (int v = threadIdx.x; v < V; v += blockDim.x) {
     const float x = l[v];
-    Stat y{x, 1.f, v, -INFINITY, 0x7fffffff};
+    Stat y{x, 1.f, v, -INFINITY, 0x7fffffff, 0.f};
     if (temperature > 0.f) {
       const uint32_t r = philox_word(static_cast<uint32_t>(v), static_cast<uint32_t>(row),
                                      static_cast<uint32_t>(row >> 32), 0xffffffffu, static_cast<uint32_t>(seed),
@@ -66,16 +61,12 @@ __global__ void __launch_bounds__(256) sample_logits_kernel(const float* __restr
       const float u = static_cast<float>(r >> 8) * (1.0f / 16777216.0f);
       y.gs = x / temperature - logf(-logf(u));
       y.garg = v;
+      y.gl = x;
     }
     st = merge(st, y);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
-           __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
-           __shfl_xor_sync(0xffffffffu, st.garg, o)};
-    st = merge(st, y);
-  }
+  for (int o = 16; o > 0; o >>= 1) st = merge(st, shfl_xor_stat(st, o));
   __shared__ Stat shared[8];
   if ((threadIdx.x & 31) == 0) shared[threadIdx.x >> 5] = st;
   __syncthreads();

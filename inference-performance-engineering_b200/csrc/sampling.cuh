@@ -31,12 +31,31 @@ __device__ __forceinline__ float uniform01(uint64_t seed, int n, int b, int64_t 
   return static_cast<float>(r >> 8) * (1.0f / 16777216.0f);
 }
 
+// Mergeable sampling statistic over a set of logits: max m, sum of exp(l - m) s, argmax arg (lowest
+// ID on ties), and the Gumbel maximum gs with its ID garg and logit gl.
 struct Stat {
   float m, s;
   int arg;
   float gs;
   int garg;
+  float gl;
 };
+
+// The neutral statistic (merging it changes nothing).
+__device__ __forceinline__ Stat empty_stat() { return Stat{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff, 0.f}; }
+
+// The statistic of lane (lane ^ o).
+__device__ __forceinline__ Stat shfl_xor_stat(const Stat& st, int o) {
+  return Stat{__shfl_xor_sync(0xffffffffu, st.m, o),   __shfl_xor_sync(0xffffffffu, st.s, o),
+              __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
+              __shfl_xor_sync(0xffffffffu, st.garg, o), __shfl_xor_sync(0xffffffffu, st.gl, o)};
+}
+
+// The record of one statistic (IPE_PARTIAL_WORDS floats): m, s, gs, gl, arg, garg as int bits.
+__device__ __forceinline__ Stat load_stat(const float* rec) {
+  return Stat{__ldcg(rec), __ldcg(rec + 1), __float_as_int(__ldcg(rec + 4)), __ldcg(rec + 2),
+              __float_as_int(__ldcg(rec + 5)), __ldcg(rec + 3)};
+}
 
 __device__ __forceinline__ Stat merge(Stat x, const Stat& y) {
   if (y.m > x.m) {
@@ -50,6 +69,7 @@ __device__ __forceinline__ Stat merge(Stat x, const Stat& y) {
   if (y.gs > x.gs || (y.gs == x.gs && y.garg < x.garg)) {
     x.gs = y.gs;
     x.garg = y.garg;
+    x.gl = y.gl;
   }
   return x;
 }

@@ -192,14 +192,15 @@ __device__ __forceinline__ void stage_rows(const bf16* src, int64_t src_stride, 
 }
 
 struct EpilogueArgs {
-  void* out;  // bf16 (store / residual in-out / silu) or fp32 logits
+  void* out;  // bf16 (store / residual in-out / silu) or fp32 (logits, partial sums)
   int64_t out_stride;
-  int rows;   // weight rows (logits: vocabulary)
+  int rows;   // weight rows (logits: this shard's vocabulary rows)
   int batch;
   float* partials;  // logits: one sampling record per row block and batch row
   const int64_t* state;
   float temperature;
   uint64_t seed;
+  int row_offset = 0;  // logits: global vocabulary ID of row 0 (a vocabulary shard)
 };
 
 // Row block rb's outputs from the complete fp32 sums acc (lane layout of mma m16n8: rows
@@ -241,6 +242,20 @@ __device__ __forceinline__ void row_block_epilogue(const float (&acc)[2][NT][4],
         const float act = bf16_round(gate / (1.0f + expf(-gate)));
         out[b * a.out_stride + col] = __float2bfloat16_rn(act * up);
       }
+  } else if constexpr (EPI == kGemvPartial) {  // fp32 sums, unrounded (a tensor-parallel shard's part)
+    float* out = static_cast<float*>(a.out);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h >= halves) break;
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = rb * 32 + (first_half + h) * 16 + g + 8 * (e >> 1);
+          const int b = 8 * j + 2 * t + (e & 1);
+          if (b < B && n < a.rows) out[b * a.out_stride + n] = acc[h][j][e];
+        }
+    }
   } else {  // fp32 logits + per-row-block sampling records
     float* logits = static_cast<float*>(a.out);
     const float temperature =
@@ -252,7 +267,7 @@ __device__ __forceinline__ void row_block_epilogue(const float (&acc)[2][NT][4],
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int b = 8 * j + 2 * t + c;
-        Stat st{-INFINITY, 0.f, 0x7fffffff, -INFINITY, 0x7fffffff};
+        Stat st = empty_stat();
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -261,27 +276,24 @@ __device__ __forceinline__ void row_block_epilogue(const float (&acc)[2][NT][4],
             if (b < B && n < a.rows) {
               const float l = bf16_round(acc[h][j][2 * r + c]);
               logits[b * a.out_stride + n] = l;
-              Stat y{l, 1.f, n, -INFINITY, 0x7fffffff};
+              const int id = n + a.row_offset;  // global vocabulary ID
+              Stat y{l, 1.f, id, -INFINITY, 0x7fffffff, 0.f};
               if (temperature > 0.f) {
-                y.gs = l / temperature - logf(-logf(uniform01(seed, n, b, step)));
-                y.garg = n;
+                y.gs = l / temperature - logf(-logf(uniform01(seed, id, b, step)));
+                y.garg = id;
+                y.gl = l;
               }
               st = merge(st, y);
             }
           }
 #pragma unroll
-        for (int o = 4; o < 32; o <<= 1) {
-          Stat y{__shfl_xor_sync(0xffffffffu, st.m, o), __shfl_xor_sync(0xffffffffu, st.s, o),
-                 __shfl_xor_sync(0xffffffffu, st.arg, o), __shfl_xor_sync(0xffffffffu, st.gs, o),
-                 __shfl_xor_sync(0xffffffffu, st.garg, o)};
-          st = merge(st, y);
-        }
+        for (int o = 4; o < 32; o <<= 1) st = merge(st, shfl_xor_stat(st, o));
         if (g == 0 && b < B) {
           float* rec = a.partials + (static_cast<int64_t>(rb) * B + b) * IPE_PARTIAL_WORDS;
           rec[0] = st.m;
           rec[1] = st.s;
           rec[2] = st.gs;
-          rec[3] = 0.f;
+          rec[3] = st.gl;
           rec[4] = __int_as_float(st.arg);
           rec[5] = __int_as_float(st.garg);
         }

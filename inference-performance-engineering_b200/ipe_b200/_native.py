@@ -15,7 +15,7 @@ from pathlib import Path
 LIBRARY = Path(__file__).resolve().parent / "lib" / "libipe_b200.so"
 
 # enum values of include/ipe_b200.h
-EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_LOGITS = 0, 1, 2, 3
+EPI_STORE, EPI_RESIDUAL, EPI_SILU_MUL, EPI_LOGITS, EPI_PARTIAL = 0, 1, 2, 3, 4
 STATE_POS, STATE_STEP, STATE_SEED, STATE_TEMPERATURE, STATE_WORDS = 0, 1, 2, 3, 8
 GATE_UP_GROUP = 64
 PARTIAL_WORDS = 8
@@ -55,6 +55,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_qk_norm_rope_append_f32": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P, _P, _P, c_int,
                                             c_float, _P]),
     "ipe_attention_f32": (c_int, [_P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int, _P]),
+    "ipe_linear_partial": (c_int, [_P, _P, _P, c_int, c_int, c_int, _P, c_size_t, _P]),
+    "ipe_add_partial": (c_int, [_P, _P, c_int64, _P]),
+    "ipe_lm_head_shard": (c_int, [_P, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_float, c_float, c_uint64,
+                                  _P, _P]),
+    "ipe_sample_records": (c_int, [_P, c_int, c_int, c_float, _P, _P, _P, c_int64, _P, _P]),
     "ipe_state_set": (c_int, [_P, c_int, c_int64, _P]),
     "ipe_state_add": (c_int, [_P, c_int, c_int64, _P]),
 }

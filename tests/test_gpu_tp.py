@@ -1,0 +1,65 @@
+"""The tensor-parallel engine on 2 GPUs (NCCL) against the single-GPU engine: teacher-forced
+logits within a few bf16 ulps (the same math; fp32 partial sums added in another order) and the
+same greedy tokens on every rank. Needs two GPUs; skipped otherwise."""
+
+import datetime
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from cases import build, to_device
+
+pytestmark = pytest.mark.gpu
+WORLD = 2
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    engine = None
+    try:
+        from ipe_b200.engine import Engine
+        from ipe_b200.tp import TensorParallelEngine
+        from oracle import qwen3 as oq
+
+        gpu = to_device(build("qwen3-1.7b-2layer"), f"cuda:{rank}")
+        ids = torch.randint(0, gpu.config.vocab_size, (2, 70), generator=torch.Generator().manual_seed(21))
+        engine = TensorParallelEngine(gpu, batch=2, capacity=96)
+        tp_logits = oq.teacher_forced(engine, ids, 64).cpu()
+        tokens, logprobs = engine.generate(ids[:, :40], 12)
+        result = {"tp_logits": tp_logits, "tokens": tokens, "logprobs": logprobs}
+        if rank == 0:
+            single = Engine(gpu, batch=2, capacity=96)
+            result["logits"] = oq.teacher_forced(single, ids, 64).cpu()
+            out = single.generate(ids[:, :40], 12)
+            result["ref_tokens"], result["ref_logprobs"] = out.tokens, out.logprobs
+        torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
+    finally:
+        engine = None  # the captured graph holds NCCL work: release it before the group goes
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
+def test_tensor_parallel_engine_matches_the_single_gpu_engine(tmp_path):
+    mp.spawn(_worker, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
+    r0, r1 = torch.load(tmp_path / "rank0.pt"), torch.load(tmp_path / "rank1.pt")
+    ref = r0["logits"]
+    for r in (r0, r1):
+        assert ((r["tp_logits"] - ref).abs() <= 4 * 2 ** -8 * ref.abs() + 0.05).all()
+        assert torch.equal(r["tokens"], r0["tokens"])  # every rank samples the same tokens
+    agree = (r0["tokens"] == r0["ref_tokens"]).float().mean()
+    assert agree > 0.9, (r0["tokens"], r0["ref_tokens"])
+    assert torch.allclose(r0["logprobs"][:, :1], r0["ref_logprobs"][:, :1], atol=0.05)
