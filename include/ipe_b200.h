@@ -238,6 +238,27 @@ int ipe_prefill_attention(const void* q, const void* k_cache, const void* v_cach
 int ipe_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epilogue,
              const void* residual, void* stream);
 
+/* ------------------------------------------------------------------ NVLink all-reduce
+ * One-shot all-reduce of tensor-parallel fp32 parts over peer memory, fused with the residual add
+ * (replaces the NCCL all-reduce + ipe_add_partial pair of a decode step). Each rank allocates one
+ * communication region (ipe_comm_alloc, ipe_comm_bytes(slot_bytes) bytes, zero-filled), exchanges
+ * its IPC handle (ipe_ipc_handle, 64 bytes) with the group, opens the peers' (ipe_ipc_open) and
+ * keeps a device array of the world region pointers, its own at index `rank`. A layer's partial
+ * product goes into this rank's slot (region + ipe_comm_slot_offset(slot, slot_bytes)); then
+ * ipe_allreduce_residual sets x[i] = bf16(x[i] + bf16(sum over ranks of slot[i])), summing in rank
+ * order so every rank gets the same bits. Consecutive calls must alternate slots 0 / 1, and every
+ * rank must make the same calls in the same order. Waits for the peers are bounded (about 2 s;
+ * then device error 3 is set and x is left unchanged). */
+size_t ipe_comm_bytes(size_t slot_bytes);
+size_t ipe_comm_slot_offset(int slot, size_t slot_bytes);
+int ipe_comm_alloc(size_t bytes, void** ptr);
+int ipe_comm_free(void* ptr);
+int ipe_ipc_handle(const void* ptr, void* handle);
+int ipe_ipc_open(const void* handle, void** ptr);
+int ipe_ipc_close(void* ptr);
+int ipe_allreduce_residual(void* x, int64_t count, const void* peers, int world, int rank, int slot,
+                           size_t slot_bytes, void* stream);
+
 /* ------------------------------------------------------------------ fp32 (plumbing) path
  * The reference at dtype float32 (TF32 disabled, src/ipe/forward.py:42-43): fp32 storage and fp32
  * FMA arithmetic, no bf16 rounding points, no tensor cores. Row-major fp32 operands; the RMSNorm

@@ -430,6 +430,53 @@ int ipe_attention_f32(const void* q, const void* k_cache, const void* v_cache, v
                      "ipe_attention_f32");
 }
 
+// ---------------------------------------------------------------- NVLink peer-memory all-reduce
+
+size_t ipe_comm_bytes(size_t slot_bytes) { return ipe::comm_region_bytes(slot_bytes); }
+
+size_t ipe_comm_slot_offset(int slot, size_t slot_bytes) {
+  return slot == 0 || slot == 1 ? ipe::comm_slot_offset(slot, slot_bytes) : 0;
+}
+
+int ipe_comm_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return fail(IPE_ERR_ARGUMENT, "ipe_comm_alloc: bad arguments");
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e == cudaSuccess) e = cudaMemset(*ptr, 0, bytes);
+  return cuda_status(e, "ipe_comm_alloc");
+}
+
+int ipe_comm_free(void* ptr) { return cuda_status(cudaFree(ptr), "ipe_comm_free"); }
+
+int ipe_ipc_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return fail(IPE_ERR_ARGUMENT, "ipe_ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e == cudaSuccess) std::memcpy(handle, &h, sizeof(h));
+  return cuda_status(e, "ipe_ipc_handle");
+}
+
+int ipe_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return fail(IPE_ERR_ARGUMENT, "ipe_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  return cuda_status(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess), "ipe_ipc_open");
+}
+
+int ipe_ipc_close(void* ptr) { return cuda_status(cudaIpcCloseMemHandle(ptr), "ipe_ipc_close"); }
+
+int ipe_allreduce_residual(void* x, int64_t count, const void* peers, int world, int rank, int slot,
+                           size_t slot_bytes, void* stream) {
+  if (!x || !peers) return fail(IPE_ERR_ARGUMENT, "ipe_allreduce_residual: null pointer");
+  if (world < 1 || world > 32 || rank < 0 || rank >= world || (slot != 0 && slot != 1))
+    return fail(IPE_ERR_ARGUMENT, "ipe_allreduce_residual: rank %d of %d, slot %d", rank, world, slot);
+  if (count < 1 || static_cast<size_t>(count) * sizeof(float) > slot_bytes)
+    return fail(IPE_ERR_ARGUMENT, "ipe_allreduce_residual: %lld values do not fit a %zu-byte slot",
+                static_cast<long long>(count), slot_bytes);
+  ipe::launch_allreduce_residual(x, count, static_cast<const uint64_t*>(peers), world, rank, slot, slot_bytes,
+                                 device_error_word(), as_stream(stream));
+  return cuda_status(cudaGetLastError(), "ipe_allreduce_residual");
+}
+
 size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capacity) {
   if (batch < 1 || q_heads < 1 || kv_heads < 1 || capacity < 1) return 0;
   return ipe::decode_step_workspace_bytes(batch, q_heads, kv_heads, capacity);

@@ -92,4 +92,10 @@ cudaError_t launch_attention_f32(const void* q, const void* k, const void* v, vo
 
 void launch_add_partial(void* x, const float* sum, int64_t count, cudaStream_t stream);
 
+// NVLink peer-memory all-reduce, allreduce.cu
+size_t comm_region_bytes(size_t slot_bytes);
+size_t comm_slot_offset(int slot, size_t slot_bytes);
+void launch_allreduce_residual(void* x, int64_t count, const uint64_t* peers, int world, int rank, int slot,
+                               size_t slot_bytes, int* err, cudaStream_t stream);
+
 }  // namespace ipe

@@ -60,6 +60,14 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_lm_head_shard": (c_int, [_P, c_int64, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_float, c_float, c_uint64,
                                   _P, _P]),
     "ipe_sample_records": (c_int, [_P, c_int, c_int, c_float, _P, _P, _P, c_int64, _P, _P]),
+    "ipe_comm_bytes": (c_size_t, [c_size_t]),
+    "ipe_comm_slot_offset": (c_size_t, [c_int, c_size_t]),
+    "ipe_comm_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p)]),
+    "ipe_comm_free": (c_int, [_P]),
+    "ipe_ipc_handle": (c_int, [_P, _P]),
+    "ipe_ipc_open": (c_int, [_P, ctypes.POINTER(c_void_p)]),
+    "ipe_ipc_close": (c_int, [_P]),
+    "ipe_allreduce_residual": (c_int, [_P, c_int64, _P, c_int, c_int, c_int, c_size_t, _P]),
     "ipe_state_set": (c_int, [_P, c_int, c_int64, _P]),
     "ipe_state_add": (c_int, [_P, c_int, c_int64, _P]),
 }

@@ -102,13 +102,64 @@ class _Layer:
         self.t_gate_up = decode_tiles(w["gate"], w["up"])
 
 
+class PeerAllReduce:
+    """The group's IPC-mapped communication regions and the fused one-shot all-reduce + residual
+    add over NVLink peer memory (ipe_allreduce_residual). Every rank of `group` constructs it (a
+    collective), and must `close()` it before the group is destroyed."""
+
+    def __init__(self, group, device: torch.device, slot_bytes: int):
+        import ctypes
+
+        lib = nat.load()
+        self.group, self.world, self.rank = group, dist.get_world_size(group), dist.get_rank(group)
+        self.slot_bytes = int(slot_bytes)
+        region = ctypes.c_void_p()
+        nat.check(lib.ipe_comm_alloc(lib.ipe_comm_bytes(self.slot_bytes), ctypes.byref(region)), "ipe_comm_alloc")
+        self.region = region.value
+        handle = (ctypes.c_char * 64)()
+        nat.check(lib.ipe_ipc_handle(self.region, handle), "ipe_ipc_handle")
+        handles: list[bytes | None] = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        pointers, self._opened = [], []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                pointers.append(self.region)
+                continue
+            peer = ctypes.c_void_p()
+            nat.check(lib.ipe_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(peer)), "ipe_ipc_open")
+            pointers.append(peer.value)
+            self._opened.append(peer.value)
+        self.table = torch.tensor(pointers, dtype=torch.int64, device=device)
+        self._slots = [self.region + int(lib.ipe_comm_slot_offset(s, self.slot_bytes)) for s in (0, 1)]
+
+    def slot(self, index: int) -> int:
+        """Device address of this rank's slot `index` (where a layer's partial product goes)."""
+        return self._slots[index]
+
+    def reduce_residual(self, x: torch.Tensor, count: int, slot: int, stream: int) -> None:
+        nat.check(nat.load().ipe_allreduce_residual(x.data_ptr(), count, self.table.data_ptr(), self.world, self.rank,
+                                                    slot, self.slot_bytes, stream), "ipe_allreduce_residual")
+
+    def close(self) -> None:
+        if self.region is None:
+            return
+        lib = nat.load()
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)  # no peer still reads this rank's region
+        for peer in self._opened:
+            nat.check(lib.ipe_ipc_close(peer), "ipe_ipc_close")
+        dist.barrier(group=self.group)
+        nat.check(lib.ipe_comm_free(self.region), "ipe_comm_free")
+        self.region, self._opened = None, []
+
+
 class TensorParallelEngine:
     """prefill / decode / generate of one batch (1..16 rows) with the model split over the ranks of
     `group` (every rank constructs it with the same arguments and calls the same methods in the
     same order). The weights in `loaded` must be bf16 on this rank's GPU; only this rank's shard is
     kept (plus the embedding and the norms, replicated)."""
 
-    def __init__(self, loaded, *, batch: int, capacity: int, group=None):
+    def __init__(self, loaded, *, batch: int, capacity: int, group=None, allreduce: str = "nvlink"):
         c, w = loaded.config, loaded.weights
         check_supported(c)
         if w.embed_tokens.dtype != torch.bfloat16 or w.embed_tokens.device.type != "cuda":
@@ -162,6 +213,18 @@ class TensorParallelEngine:
         self._warm = False
         self.batch = 0
         self.length = 0
+        if allreduce not in ("nvlink", "nccl"):
+            raise ValueError(f"allreduce {allreduce!r}: expected 'nvlink' or 'nccl'")
+        # the decode step's all-reduces: fused one-shot over NVLink peer memory, or NCCL
+        self._peer = PeerAllReduce(group, dev, batch * c.hidden_size * 4) if allreduce == "nvlink" else None
+
+    def close(self) -> None:
+        """Release the captured step and the peer-memory regions (a collective: every rank calls it
+        before the process group is destroyed)."""
+        self._graph = None
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
 
     # ----------------------------------------------------------------------------- collectives
 
@@ -301,21 +364,31 @@ class TensorParallelEngine:
                                                    self._v[index].data_ptr(), self.attn.data_ptr(), b, p.q_heads,
                                                    p.kv_heads, self.capacity, eps, self.attn_ws.data_ptr(),
                                                    self.attn_ws.numel(), stream), "ipe_decode_attention_qkv")
-            nat.check(lib.ipe_linear_partial(self.attn.data_ptr(), layer.t_o.data_ptr(), self.part.data_ptr(), b,
-                                             self.q_rows, h, lws, lwn, stream), "ipe_linear_partial o_proj")
-            self._all_reduce(self.part[:b])
-            nat.check(lib.ipe_add_partial(self.x.data_ptr(), self.part.data_ptr(), b * h, stream), "ipe_add_partial")
+            self._row_parallel(lib.ipe_linear_partial, self.attn.data_ptr(), layer.t_o.data_ptr(), self.q_rows, 0,
+                               stream)
             nat.check(lib.ipe_rmsnorm_gate_up_silu(self.x.data_ptr(), layer.post_norm.data_ptr(),
                                                    layer.t_gate_up.data_ptr(), self.act.data_ptr(), b, h, p.inter,
                                                    eps, lws, lwn, stream), "ipe_rmsnorm_gate_up_silu")
-            nat.check(lib.ipe_linear_partial(self.act.data_ptr(), layer.t_down.data_ptr(), self.part.data_ptr(), b,
-                                             p.inter, h, lws, lwn, stream), "ipe_linear_partial down_proj")
-            self._all_reduce(self.part[:b])
-            nat.check(lib.ipe_add_partial(self.x.data_ptr(), self.part.data_ptr(), b * h, stream), "ipe_add_partial")
+            self._row_parallel(lib.ipe_linear_partial, self.act.data_ptr(), layer.t_down.data_ptr(), p.inter, 1,
+                               stream)
         self._lm_head(self.x.data_ptr(), h, b, stream)
         if sample:
             self._sample(stream)
         nat.check(lib.ipe_state_add(st, nat.STATE_POS, 1, stream), "ipe_state_add")
+
+    def _row_parallel(self, partial, a_ptr: int, tiles_ptr: int, k: int, slot: int, stream: int) -> None:
+        """x += this layer's product: each rank's fp32 part (its columns of the weight), summed over
+        the ranks, rounded once, added to the residual. slot alternates 0 / 1 between calls."""
+        b, h = self.batch, self.config.hidden_size
+        lws, lwn = self.linear_ws.data_ptr(), self.linear_ws.numel()
+        out = self._peer.slot(slot) if self._peer is not None else self.part.data_ptr()
+        nat.check(partial(a_ptr, tiles_ptr, out, b, k, h, lws, lwn, stream), "ipe_linear_partial")
+        if self._peer is not None:
+            self._peer.reduce_residual(self.x, b * h, slot, stream)
+        else:
+            self._all_reduce(self.part[:b])
+            nat.check(nat.load().ipe_add_partial(self.x.data_ptr(), self.part.data_ptr(), b * h, stream),
+                      "ipe_add_partial")
 
     def _sample(self, stream: int) -> None:
         """Every rank merges every rank's records: the same token on all ranks."""

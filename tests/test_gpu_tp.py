@@ -36,10 +36,15 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
 
         gpu = to_device(build("qwen3-1.7b-2layer"), f"cuda:{rank}")
         ids = torch.randint(0, gpu.config.vocab_size, (2, 70), generator=torch.Generator().manual_seed(21))
-        engine = TensorParallelEngine(gpu, batch=2, capacity=96)
-        tp_logits = oq.teacher_forced(engine, ids, 64).cpu()
-        tokens, logprobs = engine.generate(ids[:, :40], 12)
-        result = {"tp_logits": tp_logits, "tokens": tokens, "logprobs": logprobs}
+        result = {}
+        for mode in ("nvlink", "nccl"):
+            engine = TensorParallelEngine(gpu, batch=2, capacity=96, allreduce=mode)
+            result[f"tp_logits_{mode}"] = oq.teacher_forced(engine, ids, 64).cpu()
+            result[f"tokens_{mode}"], result[f"logprobs_{mode}"] = engine.generate(ids[:, :40], 12)
+            engine.close()
+            engine = None
+        from ipe_b200 import _native as nat
+        result["device_error"] = nat.device_error()
         if rank == 0:
             single = Engine(gpu, batch=2, capacity=96)
             result["logits"] = oq.teacher_forced(single, ids, 64).cpu()
@@ -47,7 +52,8 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
             result["ref_tokens"], result["ref_logprobs"] = out.tokens, out.logprobs
         torch.save(result, os.path.join(out_dir, f"rank{rank}.pt"))
     finally:
-        engine = None  # the captured graph holds NCCL work: release it before the group goes
+        if engine is not None:  # an exception left it open: release the captured NCCL work first
+            engine._graph = None
         torch.cuda.synchronize()
         dist.destroy_process_group()
 
@@ -58,8 +64,12 @@ def test_tensor_parallel_engine_matches_the_single_gpu_engine(tmp_path):
     r0, r1 = torch.load(tmp_path / "rank0.pt"), torch.load(tmp_path / "rank1.pt")
     ref = r0["logits"]
     for r in (r0, r1):
-        assert ((r["tp_logits"] - ref).abs() <= 4 * 2 ** -8 * ref.abs() + 0.05).all()
-        assert torch.equal(r["tokens"], r0["tokens"])  # every rank samples the same tokens
-    agree = (r0["tokens"] == r0["ref_tokens"]).float().mean()
-    assert agree > 0.9, (r0["tokens"], r0["ref_tokens"])
-    assert torch.allclose(r0["logprobs"][:, :1], r0["ref_logprobs"][:, :1], atol=0.05)
+        assert r["device_error"] == 0
+        for mode in ("nvlink", "nccl"):
+            assert ((r[f"tp_logits_{mode}"] - ref).abs() <= 4 * 2 ** -8 * ref.abs() + 0.05).all()
+            assert torch.equal(r[f"tokens_{mode}"], r0[f"tokens_{mode}"])  # every rank samples the same tokens
+        # two addends sum to the same bits in either order: the peer-memory all-reduce equals NCCL's
+        assert torch.equal(r["tp_logits_nvlink"], r["tp_logits_nccl"])
+    agree = (r0["tokens_nvlink"] == r0["ref_tokens"]).float().mean()
+    assert agree > 0.9, (r0["tokens_nvlink"], r0["ref_tokens"])
+    assert torch.allclose(r0["logprobs_nvlink"][:, :1], r0["ref_logprobs"][:, :1], atol=0.05)
