@@ -316,6 +316,56 @@ def run_ours(args, rank: int, world: int) -> dict | None:
     return line
 
 
+def run_tp(args, rank: int, world: int) -> dict | None:
+    """The tensor-parallel latency case (B=1): the model split over `world` GPUs
+    (ipe_b200.tp.TensorParallelEngine, decode all-reduces over NVLink peer memory), decode tok/s of
+    the W1 generation, device time max over ranks."""
+    import torch.distributed as dist
+
+    from ipe_b200 import QWEN3_1_7B
+    from ipe_b200.synthetic import random_model
+    from ipe_b200.tp import TensorParallelEngine
+
+    batch, prompt, new, capacity, _ = WORKLOADS["W1"]
+    new = args.new_tokens or new
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    loaded = random_model(QWEN3_1_7B, seed=0, device=device, generator_device=device)
+    engine = TensorParallelEngine(loaded, batch=batch, capacity=capacity, allreduce=args.tp_allreduce)
+    ids = torch.randint(0, QWEN3_1_7B.vocab_size, (batch, prompt), generator=torch.Generator().manual_seed(0))
+    stream = torch.cuda.current_stream()
+
+    def timed(n_new: int) -> float:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        engine.generate(ids, n_new)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / 1e3
+
+    for _ in range(args.warmup):
+        timed(new)
+    with ClockSampler(device.index) as clocks:
+        full = [timed(new) for _ in range(args.steps)]
+        first = [timed(1) for _ in range(args.steps)]
+    t = torch.tensor([sum(full), sum(first)], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    engine.close()
+    if rank != 0:
+        return None
+    decode_s = (t[0] - t[1]).item()
+    value = batch * (new - 1) * args.steps / decode_s
+    return {"metric": "decode tok/s, Qwen3-1.7B bf16 B=1, tensor parallel", "value": round(value, 2),
+            "unit": "decode tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(t[0].item() / args.steps * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init N(0,0.02) weights)",
+            "config": {"workload": f"W1 tensor parallel: batch {batch}, prompt {prompt}, {new} new tokens",
+                       "parallelism": f"tp{world}", "allreduce": args.tp_allreduce},
+            "decode_ms_per_token": round(decode_s / ((new - 1) * args.steps) * 1e3, 4),
+            "clocks": clocks.summary()}
+
+
 def cpu_baseline(workload: str, samples: int) -> dict:
     """The reference engine's algorithm (oracle/ restatement, bf16, sdpa) on the host cores:
     one prefill of the workload's prompt, then `samples` decode steps (bounded sample)."""
@@ -394,6 +444,8 @@ def main() -> None:
     parser.add_argument("--cpu-decode-steps", type=int, default=8)
     parser.add_argument("--new-tokens", type=int, default=0, help="override the workload's new tokens (profiling)")
     parser.add_argument("--layers", type=int, default=0, help="fewer decoder layers (profiling only; not a bench line)")
+    parser.add_argument("--tp", action="store_true", help="tensor-parallel B=1 latency mode over the launched ranks")
+    parser.add_argument("--tp-allreduce", default="nvlink", choices=("nvlink", "nccl"))
     args = parser.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
@@ -406,7 +458,7 @@ def main() -> None:
             torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", 0)))
             dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
         try:
-            line = run_ours(args, rank, world)
+            line = run_tp(args, rank, world) if args.tp else run_ours(args, rank, world)
         finally:
             if world > 1:
                 import torch.distributed as dist

@@ -328,6 +328,19 @@ typedef struct {
   float* history_logprobs;
   int64_t history_stride;
   uint64_t* trace;                   /* nullable: per-CTA phase timestamps, see below         */
+  /* Tensor parallelism (tp_world > 1; tp_world 0 or 1 is one GPU). q_heads, kv_heads,
+   * intermediate and vocab (LM-head rows, from vocab_offset) are then this rank's shard; the
+   * weights, caches and tiles above are the shard's. o_proj and down_proj push fp32 parts into
+   * every rank's communication region (tp_peers: device array of the tp_world region pointers,
+   * ipe_decode_step_comm_bytes each, zero-filled once) and the next phase sums them, as does the
+   * sampler with every rank's LM-head records: every rank gets the same token. x_alt: a second
+   * bf16 [batch, hidden] residual buffer. Needs hidden % 256 == 0 and the activations in shared
+   * memory (batch <= 4 at Qwen3-1.7B). */
+  int tp_world, tp_rank;
+  const void* tp_peers;
+  void* x_alt;
+  int vocab_offset;                  /* first vocabulary ID of this rank's LM-head rows        */
+  int vocab_total;                   /* the full vocabulary (token IDs)                         */
 } ipe_decode_step_desc;
 
 /* Step trace (when desc.trace is set): CTA c writes globaltimer nanoseconds to
@@ -348,6 +361,8 @@ int ipe_decode_step_grid(void);
  * src/ipe/engine.py:84-111 (decode -> _step) and, with sampling, one iteration of
  * src/ipe/engine.py:137-147. */
 int ipe_decode_step(const ipe_decode_step_desc* desc, void* stream);
+/* Bytes of one rank's communication region for a tensor-parallel decode step. */
+size_t ipe_decode_step_comm_bytes(int tp_world, int batch, int hidden, int vocab_rows_max);
 size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capacity);
 
 /* ------------------------------------------------------------------ step state */

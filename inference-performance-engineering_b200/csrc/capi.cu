@@ -484,6 +484,11 @@ size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capac
 
 int ipe_decode_step_grid(void) { return ipe::sm_count(); }
 
+size_t ipe_decode_step_comm_bytes(int tp_world, int batch, int hidden, int vocab_rows_max) {
+  if (tp_world < 1 || batch < 1 || hidden < 1 || vocab_rows_max < 1) return 0;
+  return ipe::decode_step_comm_bytes(tp_world, batch, hidden, vocab_rows_max);
+}
+
 int ipe_decode_step(const ipe_decode_step_desc* d, void* stream) {
   if (!d) return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: null descriptor");
   if (!d->layer_descs || !d->embed || !d->lm_head_tiles || !d->final_norm || !d->cos_table || !d->sin_table ||
@@ -504,6 +509,10 @@ int ipe_decode_step(const ipe_decode_step_desc* d, void* stream) {
     return fail(IPE_ERR_UNSUPPORTED, "ipe_decode_step: hidden / intermediate must be multiples of 128, vocab of 32");
   if (d->history_tokens && (!d->history_logprobs || d->history_stride < 1))
     return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: history needs logprobs and a stride");
+  if (d->tp_world > 1 && (d->tp_world > 32 || d->tp_rank < 0 || d->tp_rank >= d->tp_world || !d->tp_peers ||
+                         !d->x_alt || !aligned16(d->x_alt) || d->vocab_total < d->vocab || d->vocab_offset < 0 ||
+                         d->vocab_offset % 32))
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: tensor-parallel fields");
   if (d->workspace_bytes < ipe_decode_step_workspace(d->batch, d->q_heads, d->kv_heads, d->capacity))
     return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: workspace of %zu bytes needed",
                 ipe_decode_step_workspace(d->batch, d->q_heads, d->kv_heads, d->capacity));

@@ -40,7 +40,7 @@ constexpr int kThreads = 32 * (kConsumers + 1);
 constexpr int kCThreads = 32 * kConsumers;
 constexpr int kPad = 32;
 constexpr int kStepBarrier = 1;  // named barrier id of the consumer warps
-constexpr size_t kSmemMax = 227 * 1024;
+constexpr size_t kSmemMax = 226 * 1024;  // dynamic shared memory; the rest holds static arrays
 
 struct StepArgs {
   ipe_decode_step_desc d;
@@ -53,6 +53,10 @@ struct StepArgs {
   unsigned prefetch_bytes;  // how far the L2 prefetch runs ahead of the shared-memory copies
   int evict_first;          // weight copies mark their L2 lines evict-first
   int halves;               // half-row-block units allowed
+  // tensor parallelism (d.tp_world > 1): byte offsets in a communication region
+  size_t recv_x;            // [2 slots][world][batch][hidden] fp32 parts of o_proj / down_proj
+  size_t recv_rec;          // [world][parts_max][batch][IPE_PARTIAL_WORDS] LM-head records
+  int parts_max;            // LM-head records per rank (the largest shard's)
 };
 
 __device__ __forceinline__ void consumers_sync() {
@@ -95,6 +99,76 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
     }
     __threadfence();
     if (trace) trace[2 + 5 * (index - 1)] = globaltimer_ns();
+  }
+  consumers_sync();
+  return *abort_smem == 0;
+}
+
+// --------------------------------------------------------------------- tensor parallelism
+// Communication region of a rank (see ipe_decode_step_comm_bytes): u32 flag[r] at byte 4 r (the
+// last epoch rank r announced here), the epoch counter at byte 128, then the receive buffers.
+constexpr size_t kTpFlags = 0;
+constexpr size_t kTpCounter = 128;
+constexpr size_t kTpRecv = 256;
+
+__device__ __forceinline__ unsigned char* tp_region(const ipe_decode_step_desc& d, int r) {
+  return reinterpret_cast<unsigned char*>(static_cast<const uint64_t*>(d.tp_peers)[r]);
+}
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// A grid barrier that is also an exchange with the other ranks: every CTA makes its pushes to the
+// peers visible and arrives; CTA 0, once all have arrived, announces `epoch` to every peer and
+// waits (bounded) for every peer's announcement, then releases this GPU's CTAs. After it, every
+// rank's pushes of the phase are in this rank's receive buffers. epoch matters in CTA 0 only.
+__device__ bool grid_sync_tp(const StepArgs& a, unsigned index, int tid, int* abort_smem, unsigned epoch) {
+  consumers_sync();
+  if (tid == 0) {
+    const ipe_decode_step_desc& d = a.d;
+    __threadfence_system();
+    atomicAdd(&a.grid_bar[0], 1u);
+    bool ok = true;
+    uint64_t start = 0;
+    auto waiting = [&](unsigned i) {  // false once the step is aborted or the wait limit passed
+      __nanosleep(32);
+      if ((i & 63u) != 63u) return true;
+      if (ld_acquire(&a.grid_bar[1])) return false;
+      const uint64_t now = globaltimer_ns();
+      if (start == 0) start = now;
+      else if (now - start > kWaitLimitNs) {
+        report(a.err, kErrWaitTimeout);
+        atomicExch(&a.grid_bar[1], 1u);
+        return false;
+      }
+      return true;
+    };
+    if (blockIdx.x == 0) {
+      const unsigned target = index * gridDim.x;
+      for (unsigned i = 0; ok && ld_acquire(&a.grid_bar[0]) < target; ++i) ok = waiting(i);
+      if (ok) {
+        __threadfence_system();
+        for (int r = 0; r < d.tp_world; ++r)
+          if (r != d.tp_rank) st_release_sys(reinterpret_cast<unsigned*>(tp_region(d, r) + kTpFlags) + d.tp_rank, epoch);
+        const unsigned* flags = reinterpret_cast<const unsigned*>(tp_region(d, d.tp_rank) + kTpFlags);
+        for (int r = 0; r < d.tp_world && ok; ++r) {
+          if (r == d.tp_rank) continue;
+          for (unsigned i = 0; ok && static_cast<int>(ld_acquire_sys(flags + r) - epoch) < 0; ++i) ok = waiting(i);
+        }
+      }
+      if (ok) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&a.grid_bar[2]), "r"(index) : "memory");
+    } else {
+      for (unsigned i = 0; ok && ld_acquire(&a.grid_bar[2]) < index; ++i) ok = waiting(i);
+    }
+    if (!ok) *abort_smem = 1;
+    __threadfence();
   }
   consumers_sync();
   return *abort_smem == 0;
@@ -308,6 +382,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   auto mark = [&](int k) {
     if (trace && tid == 0) trace[1 + 5 * (barrier_index - 1) + k] = globaltimer_ns();
   };
+  // tensor parallelism: this rank's region, and the epoch of its exchanges (CTA 0, thread 0)
+  const bool tp = d.tp_world > 1;
+  unsigned char* my_region = tp ? tp_region(d, d.tp_rank) : nullptr;
+  unsigned tp_epoch = (tp && blockIdx.x == 0 && tid == 0) ? *reinterpret_cast<const unsigned*>(my_region + kTpCounter) : 0u;
+  const size_t x_part_bytes = static_cast<size_t>(B) * H * sizeof(float);
+  const size_t rec_rank_bytes = static_cast<size_t>(a.parts_max) * B * IPE_PARTIAL_WORDS * sizeof(float);
+  __shared__ float red_ss[4 * 16];  // tensor-parallel staging: [warp][row] sums of squares
+  int tp_slot = 0;                  // receive slot of the current row-parallel phase
 
   // Embedding: x[b] = embed[tokens[b]] (out-of-range IDs give zeros and set device error 1).
   {
@@ -317,7 +399,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       const int b = i / vecs, v = i % vecs;
       const int64_t id = d.tokens[b];
       uint4 val = make_uint4(0, 0, 0, 0);
-      if (id >= 0 && id < d.vocab) val = ldg16(static_cast<const bf16*>(d.embed) + id * H + v * 8);
+      if (id >= 0 && id < (d.vocab_total > 0 ? d.vocab_total : d.vocab))
+        val = ldg16(static_cast<const bf16*>(d.embed) + id * H + v * 8);
       else if (v == 0) report(a.err, kErrTokenRange);
       *reinterpret_cast<uint4*>(x + static_cast<int64_t>(b) * H + v * 8) = val;
     }
@@ -330,6 +413,94 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     stage_rows(src, K, norm_w, d.eps, B, K, xs, K + kPad, rstd, cw, kConsumers, lane, ACT_SMEM);
     consumers_sync();
     mark(2);
+  };
+
+  // (tensor parallel) The residual stream after a row-parallel layer, x = bf16(x_old + bf16(sum
+  // over the ranks, in rank order, of the parts in receive slot `slot`)) (slot < 0: x_old as is),
+  // staged in shared memory, RMS-normalised with norm_w when non-null; chunk i of it also goes to
+  // x_new (when non-null) from CTA i % grid, so the next residual base is whole after the next
+  // barrier. Every CTA runs it, with or without units. Needs hidden % 256 == 0.
+  auto stage_tp = [&](const bf16* x_old, bf16* x_new, int slot, const bf16* norm_w) {
+    const int chunks = H / 8, total = B * chunks;
+    const float* parts = slot >= 0 ? reinterpret_cast<const float*>(my_region + a.recv_x + slot * d.tp_world * x_part_bytes)
+                                   : nullptr;
+    if (norm_w && lane == 0)
+      for (int b = 0; b < B; ++b) red_ss[cw * 16 + b] = 0.f;
+    for (int i = tid; i < total; i += kCThreads) {  // warp-uniform rows: chunks is a multiple of 32
+      const int b = i / chunks, c = i % chunks;
+      float f[8];
+      unpack8(ldcg16(x_old + static_cast<int64_t>(b) * H + c * 8), f);
+      if (parts) {
+        float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        for (int r = 0; r < d.tp_world; ++r) {
+          const float4* q = reinterpret_cast<const float4*>(parts + (static_cast<int64_t>(r) * B + b) * H + c * 8);
+          const float4 lo = __ldcv(q), hi = __ldcv(q + 1);  // pushed by the peers: read fresh
+          sum[0] += lo.x; sum[1] += lo.y; sum[2] += lo.z; sum[3] += lo.w;
+          sum[4] += hi.x; sum[5] += hi.y; sum[6] += hi.z; sum[7] += hi.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = bf16_round(f[e] + bf16_round(sum[e]));
+      }
+      const uint4 packed = pack8(f);
+      if (x_new && i % G_ == static_cast<int>(blockIdx.x))
+        *reinterpret_cast<uint4*>(x_new + static_cast<int64_t>(b) * H + c * 8) = packed;
+      *reinterpret_cast<uint4*>(xs + b * (H + kPad) + c * 8) = packed;
+      if (norm_w) {
+        float sq = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) sq += f[e] * f[e];
+        sq = warp_sum(sq);
+        if (lane == 0) red_ss[cw * 16 + b] += sq;
+      }
+    }
+    if (norm_w) {
+      consumers_sync();
+      for (int i = tid; i < total; i += kCThreads) {
+        const int b = i / chunks, c = i % chunks;
+        const float r = rsqrtf((red_ss[b] + red_ss[16 + b] + red_ss[32 + b] + red_ss[48 + b]) / static_cast<float>(H) +
+                               d.eps);
+        float f[8], w[8];
+        unpack8(*reinterpret_cast<const uint4*>(xs + b * (H + kPad) + c * 8), f);
+        unpack8(ldg16(norm_w + c * 8), w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = w[e] * bf16_round(f[e] * r);
+        *reinterpret_cast<uint4*>(xs + b * (H + kPad) + c * 8) = pack8(f);
+      }
+    }
+    consumers_sync();
+    mark(2);
+  };
+
+  // (tensor parallel) A row-parallel unit's fp32 sums into every rank's receive slot tp_slot.
+  auto push_parts = [&](const float (&acc)[2][NT][4], int rb, int first_half, int halves) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      if (h >= halves) break;
+#pragma unroll
+      for (int j = 0; j < NT; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int n = rb * 32 + (first_half + h) * 16 + g + 8 * (e >> 1);
+          const int b = 8 * j + 2 * t + (e & 1);
+          if (b >= B || n >= H) continue;
+          for (int r = 0; r < d.tp_world; ++r) {
+            float* dst = reinterpret_cast<float*>(tp_region(d, r) + a.recv_x +
+                                                  (static_cast<size_t>(tp_slot) * d.tp_world + d.tp_rank) * x_part_bytes);
+            dst[b * H + n] = acc[h][j][e];
+          }
+        }
+    }
+  };
+
+  // (tensor parallel) The LM-head records of row block rb into every rank's record buffer.
+  auto push_records = [&](int rb) {
+    __syncwarp();
+    for (int l = lane; l < B * IPE_PARTIAL_WORDS; l += 32) {
+      const int64_t index = static_cast<int64_t>(rb) * B * IPE_PARTIAL_WORDS + l;
+      const float v = d.partials[index];
+      for (int r = 0; r < d.tp_world; ++r)
+        reinterpret_cast<float*>(tp_region(d, r) + a.recv_rec + d.tp_rank * rec_rank_bytes)[index] = v;
+    }
   };
 
   // One weight phase: this CTA's units, tiles round-robin over the consumer warps.
@@ -414,11 +585,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
 #pragma unroll
               for (int e = 0; e < 4; ++e) acc[h][j][e] += other[(h * NT + j) * 4 + e];
         }
-        if (ph.half) {
+        if (EPI == kGemvResidual && tp) {  // a row-parallel layer: push this rank's part
+          if (ph.half) push_parts(acc, u >> 1, u & 1, 1);
+          else push_parts(acc, u, 0, 2);
+        } else if (ph.half) {
           if constexpr (EPI == kGemvStore || EPI == kGemvResidual)
             row_block_epilogue<EPI, NT>(acc, u >> 1, lane, ea, u & 1, 1);
         } else {
           row_block_epilogue<EPI, NT>(acc, u, lane, ea);
+          if (EPI == kGemvLogits && tp) push_records(u);
         }
       }
       consumers_sync();
@@ -446,8 +621,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
 
   for (int layer = 0; layer < d.layers; ++layer) {
     const ipe_layer_desc& L = d.layer_descs[layer];
-    // QKV projection (input RMSNorm fused)
-    stage(x, static_cast<const bf16*>(L.input_layernorm), H);
+    // QKV projection (input RMSNorm fused); tensor parallel: after the previous layer's down_proj
+    // parts, the residual stream moves from x to x_alt
+    if (tp) stage_tp(x, static_cast<bf16*>(d.x_alt), layer == 0 ? -1 : 1, static_cast<const bf16*>(L.input_layernorm));
+    else stage(x, static_cast<const bf16*>(L.input_layernorm), H);
     if (!run_phase(EpiStore{}, phase_shape(layer, 0), x, static_cast<const bf16*>(L.input_layernorm), H,
                    EpilogueArgs{qkv, QKV, QKV, B, nullptr, nullptr, 0.f, 0}))
       return;
@@ -482,48 +659,86 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       }
     }
     if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
-    // o_proj + residual
+    // o_proj + residual (tensor parallel: this rank's part, pushed to every rank)
     stage(attn, nullptr, Q);
+    tp_slot = 0;
     if (!run_phase(EpiResidual{}, phase_shape(layer, 1), attn, nullptr, Q,
                    EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
-    // post-attention RMSNorm + gate/up + SiLU * up
-    stage(x, static_cast<const bf16*>(L.post_attention_layernorm), H);
+    if (!(tp ? grid_sync_tp(a, ++barrier_index, tid, abort_smem, ++tp_epoch)
+             : grid_sync(a, ++barrier_index, tid, abort_smem, trace)))
+      return;
+    // post-attention RMSNorm + gate/up + SiLU * up (tensor parallel: the residual stream moves back
+    // from x_alt to x with the o_proj parts)
+    if (tp) stage_tp(static_cast<const bf16*>(d.x_alt), x, 0, static_cast<const bf16*>(L.post_attention_layernorm));
+    else stage(x, static_cast<const bf16*>(L.post_attention_layernorm), H);
     if (!run_phase(EpiSilu{}, phase_shape(layer, 2), x, static_cast<const bf16*>(L.post_attention_layernorm), H,
                    EpilogueArgs{act, I, 2 * I, B, nullptr, nullptr, 0.f, 0}))
       return;
     if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
-    // down_proj + residual
+    // down_proj + residual (tensor parallel: this rank's part, pushed to every rank)
     stage(act, nullptr, I);
+    tp_slot = 1;
     if (!run_phase(EpiResidual{}, phase_shape(layer, 3), act, nullptr, I,
                    EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
+    if (!(tp ? grid_sync_tp(a, ++barrier_index, tid, abort_smem, ++tp_epoch)
+             : grid_sync(a, ++barrier_index, tid, abort_smem, trace)))
+      return;
   }
   // final RMSNorm + tied LM head: fp32 logits and one sampling record per 32 vocabulary rows
-  stage(x, static_cast<const bf16*>(d.final_norm), H);
-  if (!run_phase(EpiLogits{}, phase_shape(d.layers, 0), x, static_cast<const bf16*>(d.final_norm), H,
-                 EpilogueArgs{d.logits, d.vocab, d.vocab, B, d.partials, state, 0.f, 0}))
+  // (tensor parallel: this rank's vocabulary rows, records pushed to every rank)
+  if (tp) {
+    stage_tp(x, nullptr, 1, static_cast<const bf16*>(d.final_norm));
+    // neutral records for this rank's padding up to the largest shard's record count
+    const int parts_mine = (d.vocab + 31) / 32;
+    for (int l = tid; l < (a.parts_max - parts_mine) * B; l += kCThreads) {
+      if (blockIdx.x != 0) break;
+      const int64_t index = (static_cast<int64_t>(parts_mine) * B + l) * IPE_PARTIAL_WORDS;
+      const float rec[IPE_PARTIAL_WORDS] = {-INFINITY, 0.f, -INFINITY, 0.f, __int_as_float(0x7fffffff),
+                                            __int_as_float(0x7fffffff), 0.f, 0.f};
+      for (int r = 0; r < d.tp_world; ++r)
+        for (int w = 0; w < IPE_PARTIAL_WORDS; ++w)
+          reinterpret_cast<float*>(tp_region(d, r) + a.recv_rec + d.tp_rank * rec_rank_bytes)[index + w] = rec[w];
+    }
+  } else {
+    stage(x, static_cast<const bf16*>(d.final_norm), H);
+  }
+  {
+    EpilogueArgs ea{d.logits, d.vocab, d.vocab, B, d.partials, state, 0.f, 0};
+    ea.row_offset = d.vocab_offset;
+    if (!run_phase(EpiLogits{}, phase_shape(d.layers, 0), x, static_cast<const bf16*>(d.final_norm), H, ea)) return;
+  }
+  if (!(tp ? grid_sync_tp(a, ++barrier_index, tid, abort_smem, ++tp_epoch)
+           : grid_sync(a, ++barrier_index, tid, abort_smem, trace)))
     return;
-  if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
   if (trace && tid == 0) trace[IPE_TRACE_WORDS(d.layers) - 1] = globaltimer_ns();
   if (blockIdx.x != 0) return;
 
   // Sampling (CTA 0): token and untempered log-probability per row, fed back as the next input.
-  const int parts = (d.vocab + 31) / 32;
+  // Tensor parallel: over every rank's records (the same on every rank); the chosen token's logit
+  // then comes from the records.
+  const int parts = tp ? d.tp_world * a.parts_max : (d.vocab + 31) / 32;
+  const float* records = tp ? reinterpret_cast<const float*>(my_region + a.recv_rec) : d.partials;
   if (d.history_tokens) {
     const float temperature = __int_as_float(static_cast<int>(state[IPE_STATE_TEMPERATURE]));
     const int64_t step = state[IPE_STATE_STEP];
     for (int b = cw; b < B; b += kConsumers) {
       Stat st = empty_stat();
       for (int p = lane; p < parts; p += 32)
-        st = merge(st, load_stat(d.partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
+        st = merge(st, tp ? Stat{__ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS),
+                                 __ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 1),
+                                 __float_as_int(__ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 4)),
+                                 __ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 2),
+                                 __float_as_int(__ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 5)),
+                                 __ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 3)}
+                          : load_stat(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) st = merge(st, shfl_xor_stat(st, o));
       if (lane == 0) {
         const int token = temperature > 0.f ? st.garg : st.arg;
-        const float logit = __ldcg(d.logits + static_cast<int64_t>(b) * d.vocab + token);
+        const float logit = tp ? (temperature > 0.f ? st.gl : st.m)
+                               : __ldcg(d.logits + static_cast<int64_t>(b) * d.vocab + token);
         d.history_tokens[b * d.history_stride + step] = token;
         d.history_logprobs[b * d.history_stride + step] = (logit - st.m) - logf(st.s);
         d.tokens[b] = token;
@@ -534,6 +749,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   if (tid == 0) {
     if (d.history_tokens) state[IPE_STATE_STEP] += 1;
     state[IPE_STATE_POS] = pos + 1;
+    if (tp) *reinterpret_cast<unsigned*>(my_region + kTpCounter) = tp_epoch;  // the exchanges of the next step
   }
 }
 
@@ -612,6 +828,12 @@ size_t attn_bytes(int group) {
 
 }  // namespace
 
+size_t decode_step_comm_bytes(int world, int batch, int hidden, int vocab_rows_max) {
+  const size_t parts_max = (static_cast<size_t>(vocab_rows_max) + 31) / 32;
+  const size_t recv_x = (2ull * world * batch * hidden * sizeof(float) + 255) / 256 * 256;
+  return 256 + recv_x + static_cast<size_t>(world) * parts_max * batch * IPE_PARTIAL_WORDS * sizeof(float);
+}
+
 size_t decode_step_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity) {
   (void)capacity;  // attention records are per split, at most kAttnSplitsMax of them
   const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int) + 255) / 256 * 256;
@@ -647,8 +869,18 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
     *message = "decode-step scratch does not fit in shared memory";
     return cudaErrorInvalidValue;
   }
-  // the grid barrier counts arrivals from zero every step
-  cudaError_t e = cudaMemsetAsync(a.grid_bar, 0, 2 * sizeof(unsigned), stream);
+  if (d.tp_world > 1) {
+    if (!act_smem || d.hidden % 256) {
+      *message = "tensor parallel: needs hidden % 256 == 0 and the activations in shared memory (a smaller batch)";
+      return cudaErrorInvalidValue;
+    }
+    const int blocks = (d.vocab_total + 31) / 32;
+    a.parts_max = (blocks + d.tp_world - 1) / d.tp_world;
+    a.recv_x = 256;
+    a.recv_rec = a.recv_x + (2ull * d.tp_world * d.batch * d.hidden * sizeof(float) + 255) / 256 * 256;
+  }
+  // the grid barrier counts arrivals from zero every step ([0] arrivals, [1] abort, [2] release)
+  cudaError_t e = cudaMemsetAsync(a.grid_bar, 0, 4 * sizeof(unsigned), stream);
   if (e != cudaSuccess) return e;
   if (nt == 1) return act_smem ? by_group<1, true>(a, smem, stream) : by_group<1, false>(a, smem, stream);
   return act_smem ? by_group<2, true>(a, smem, stream) : by_group<2, false>(a, smem, stream);

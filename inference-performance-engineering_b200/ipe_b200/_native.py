@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_decode_step": (c_int, [ctypes.c_void_p, _P]),
     "ipe_decode_step_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ipe_decode_step_grid": (c_int, []),
+    "ipe_decode_step_comm_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ipe_gemm_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P]),
     "ipe_embed_f32": (c_int, [_P, c_int64, _P, c_int64, c_int, _P, _P]),
     "ipe_qk_norm_rope_append_f32": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P, _P, _P, c_int,
@@ -91,7 +92,8 @@ class StepDesc(ctypes.Structure):
                 ("x", c_void_p), ("qkv", c_void_p), ("attn", c_void_p), ("act", c_void_p), ("logits", c_void_p),
                 ("partials", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
                 ("history_tokens", c_void_p), ("history_logprobs", c_void_p), ("history_stride", c_int64),
-                ("trace", c_void_p)]
+                ("trace", c_void_p), ("tp_world", c_int), ("tp_rank", c_int), ("tp_peers", c_void_p),
+                ("x_alt", c_void_p), ("vocab_offset", c_int), ("vocab_total", c_int)]
 
 
 def trace_words(layers: int) -> int:

@@ -264,6 +264,7 @@ def step_desc(model: PackedModel, buf: DecodeBuffers, descs: torch.Tensor, batch
     d.q_heads, d.kv_heads, d.vocab, d.capacity, d.batch = (c.num_attention_heads, c.num_key_value_heads,
                                                            c.vocab_size, capacity, batch)
     d.eps = c.rms_norm_eps
+    d.vocab_total, d.tp_world = c.vocab_size, 1
     d.layer_descs = descs.data_ptr()
     d.embed, d.lm_head_tiles, d.final_norm = model.embed.data_ptr(), model.t_lm_head.data_ptr(), model.final_norm.data_ptr()
     d.cos_table, d.sin_table = cos.data_ptr(), sin.data_ptr()

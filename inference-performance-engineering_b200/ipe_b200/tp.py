@@ -12,8 +12,17 @@ all-reduce sums the parts and `ipe_add_partial` applies the residual with the si
 of the unsplit layer, so the math is the unsharded engine's up to fp32 summation order. The LM
 head shard writes sampling records with global vocabulary IDs (and the winning logit); an
 all-gather of the records lets every rank sample the same token (`ipe_sample_records`), keeping
-the ranks in lock step without moving logits. A decode step is the per-operator kernels plus
-2 * layers all-reduces and one all-gather, captured once in a CUDA graph.
+the ranks in lock step without moving logits.
+
+A decode step runs one of three ways (`allreduce`):
+- "fused" (default): the one-kernel decode step (ipe_decode_step) with the exchanges inside it.
+  Each row-parallel unit pushes its fp32 sums straight into every rank's receive buffer over
+  NVLink; the grid barrier after the phase is also a cross-rank flag exchange; the next phase's
+  staging sums the parts in rank order, applies the residual and the RMSNorm. The LM-head
+  records go to every rank the same way and every rank samples the same token in the kernel.
+- "nvlink": the per-operator kernels with a one-shot all-reduce kernel over peer memory.
+- "nccl": the per-operator kernels with NCCL all-reduces and an all-gather of the records.
+The two per-operator modes are captured once in a CUDA graph, as is the fused step.
 """
 
 from __future__ import annotations
@@ -107,14 +116,17 @@ class PeerAllReduce:
     add over NVLink peer memory (ipe_allreduce_residual). Every rank of `group` constructs it (a
     collective), and must `close()` it before the group is destroyed."""
 
-    def __init__(self, group, device: torch.device, slot_bytes: int):
+    def __init__(self, group, device: torch.device, slot_bytes: int, region_bytes: int | None = None):
+        """slot_bytes: the largest part one all-reduce moves. region_bytes: allocate a region of
+        this size instead (the fused decode step's layout, ipe_decode_step_comm_bytes)."""
         import ctypes
 
         lib = nat.load()
         self.group, self.world, self.rank = group, dist.get_world_size(group), dist.get_rank(group)
         self.slot_bytes = int(slot_bytes)
+        size = int(region_bytes) if region_bytes is not None else int(lib.ipe_comm_bytes(self.slot_bytes))
         region = ctypes.c_void_p()
-        nat.check(lib.ipe_comm_alloc(lib.ipe_comm_bytes(self.slot_bytes), ctypes.byref(region)), "ipe_comm_alloc")
+        nat.check(lib.ipe_comm_alloc(size, ctypes.byref(region)), "ipe_comm_alloc")
         self.region = region.value
         handle = (ctypes.c_char * 64)()
         nat.check(lib.ipe_ipc_handle(self.region, handle), "ipe_ipc_handle")
@@ -159,7 +171,7 @@ class TensorParallelEngine:
     same order). The weights in `loaded` must be bf16 on this rank's GPU; only this rank's shard is
     kept (plus the embedding and the norms, replicated)."""
 
-    def __init__(self, loaded, *, batch: int, capacity: int, group=None, allreduce: str = "nvlink"):
+    def __init__(self, loaded, *, batch: int, capacity: int, group=None, allreduce: str = "fused"):
         c, w = loaded.config, loaded.weights
         check_supported(c)
         if w.embed_tokens.dtype != torch.bfloat16 or w.embed_tokens.device.type != "cuda":
@@ -213,10 +225,22 @@ class TensorParallelEngine:
         self._warm = False
         self.batch = 0
         self.length = 0
-        if allreduce not in ("nvlink", "nccl"):
-            raise ValueError(f"allreduce {allreduce!r}: expected 'nvlink' or 'nccl'")
-        # the decode step's all-reduces: fused one-shot over NVLink peer memory, or NCCL
-        self._peer = PeerAllReduce(group, dev, batch * c.hidden_size * 4) if allreduce == "nvlink" else None
+        if allreduce not in ("fused", "nvlink", "nccl"):
+            raise ValueError(f"allreduce {allreduce!r}: expected 'fused', 'nvlink' or 'nccl'")
+        # the decode step's all-reduces: inside the one-kernel decode step ("fused"), one-shot kernels
+        # over NVLink peer memory ("nvlink"), or NCCL
+        self.allreduce = allreduce
+        self._peer = None
+        if allreduce == "nvlink":
+            self._peer = PeerAllReduce(group, dev, batch * c.hidden_size * 4)
+        elif allreduce == "fused":
+            region = int(lib.ipe_decode_step_comm_bytes(self.world, batch, c.hidden_size, 32 * p.parts_max))
+            self._peer = PeerAllReduce(group, dev, 0, region_bytes=region)
+            self.x_alt = torch.empty_like(self.x)
+            self.step_ws = torch.zeros(int(lib.ipe_decode_step_workspace(batch, p.q_heads, p.kv_heads, capacity)),
+                                       dtype=torch.uint8, device=dev)
+            self._layer_descs = self._make_layer_descs()
+            self._descs: dict[tuple[int, bool], nat.StepDesc] = {}
 
     def close(self) -> None:
         """Release the captured step and the peer-memory regions (a collective: every rank calls it
@@ -225,6 +249,51 @@ class TensorParallelEngine:
         if self._peer is not None:
             self._peer.close()
             self._peer = None
+
+    # ------------------------------------------------------------------------ one-kernel step
+
+    def _make_layer_descs(self) -> torch.Tensor:
+        """The device array of ipe_layer_desc over this rank's shard tiles and KV cache."""
+        import ctypes
+
+        descs = (nat.LayerDesc * len(self.layers))()
+        for i, layer in enumerate(self.layers):
+            fields = tuple(t.data_ptr() for t in (layer.in_norm, layer.post_norm, layer.q_norm, layer.k_norm,
+                                                  layer.t_qkv, layer.t_o, layer.t_gate_up, layer.t_down,
+                                                  self._k[i], self._v[i]))
+            if any(f % 16 for f in fields):
+                raise ValueError(f"layer {i}: the decode step needs 16-byte aligned operands")
+            descs[i] = nat.LayerDesc(*fields)
+        raw = torch.frombuffer(bytearray(ctypes.string_at(ctypes.addressof(descs), ctypes.sizeof(descs))),
+                               dtype=torch.uint8)
+        return raw.to(self.device)
+
+    def _step_desc(self, sample: bool) -> nat.StepDesc:
+        """ipe_decode_step_desc of this rank's shard: the decode step with its row-parallel sums and
+        the LM-head records exchanged inside the kernel over the peers' regions."""
+        key = (self.batch, sample)
+        d = self._descs.get(key)
+        if d is not None:
+            return d
+        c, p = self.config, self.plan
+        d = nat.StepDesc()
+        d.layers, d.hidden, d.intermediate = c.num_hidden_layers, c.hidden_size, p.inter
+        d.q_heads, d.kv_heads, d.vocab, d.capacity, d.batch = p.q_heads, p.kv_heads, p.vocab_rows, self.capacity, self.batch
+        d.eps = c.rms_norm_eps
+        d.layer_descs = self._layer_descs.data_ptr()
+        d.embed, d.lm_head_tiles, d.final_norm = self.embed.data_ptr(), self.t_lm.data_ptr(), self.final_norm.data_ptr()
+        d.cos_table, d.sin_table = self._cos.data_ptr(), self._sin.data_ptr()
+        d.state, d.tokens = self.state.data_ptr(), self.tokens.data_ptr()
+        d.x, d.qkv, d.attn, d.act = self.x.data_ptr(), self.qkv.data_ptr(), self.attn.data_ptr(), self.act.data_ptr()
+        d.logits, d.partials = self.logits.data_ptr(), self.partials.data_ptr()
+        d.workspace, d.workspace_bytes = self.step_ws.data_ptr(), self.step_ws.numel()
+        if sample:
+            d.history_tokens, d.history_logprobs = self.history_tokens.data_ptr(), self.history_logprobs.data_ptr()
+            d.history_stride = self.history_tokens.shape[1]
+        d.tp_world, d.tp_rank, d.tp_peers = self.world, p.rank, self._peer.table.data_ptr()
+        d.x_alt, d.vocab_offset, d.vocab_total = self.x_alt.data_ptr(), p.vocab_offset, c.vocab_size
+        self._descs[key] = d
+        return d
 
     # ----------------------------------------------------------------------------- collectives
 
@@ -350,6 +419,11 @@ class TensorParallelEngine:
         """One decode step at state[POS] for the rows in self.tokens; with `sample`, the next token
         goes to the history at state[STEP] and to self.tokens, and STEP advances."""
         c, p, lib = self.config, self.plan, nat.load()
+        if self.allreduce == "fused":
+            import ctypes
+
+            nat.check(lib.ipe_decode_step(ctypes.addressof(self._step_desc(sample)), stream), "ipe_decode_step")
+            return
         b, h, eps, st = self.batch, c.hidden_size, c.rms_norm_eps, self.state.data_ptr()
         lws, lwn = self.linear_ws.data_ptr(), self.linear_ws.numel()
         nat.check(lib.ipe_embed(self.tokens.data_ptr(), b, self.embed.data_ptr(), c.vocab_size, h, self.x.data_ptr(),

@@ -1,6 +1,8 @@
-"""The tensor-parallel engine on 2 GPUs (NCCL) against the single-GPU engine: teacher-forced
-logits within a few bf16 ulps (the same math; fp32 partial sums added in another order) and the
-same greedy tokens on every rank. Needs two GPUs; skipped otherwise."""
+"""The tensor-parallel engine on 2 GPUs in its three step modes (the one-kernel step with its
+exchanges inside, per-operator kernels with the peer-memory all-reduce, and with NCCL) against the
+single-GPU engine: teacher-forced logits within a few bf16 ulps (the same math; fp32 partial sums
+added in another order) and the same greedy tokens on every rank. Needs two GPUs; skipped
+otherwise."""
 
 import datetime
 import os
@@ -15,6 +17,7 @@ from cases import build, to_device
 
 pytestmark = pytest.mark.gpu
 WORLD = 2
+MODES = ("fused", "nvlink", "nccl")
 
 
 def _free_port() -> int:
@@ -37,7 +40,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         gpu = to_device(build("qwen3-1.7b-2layer"), f"cuda:{rank}")
         ids = torch.randint(0, gpu.config.vocab_size, (2, 70), generator=torch.Generator().manual_seed(21))
         result = {}
-        for mode in ("nvlink", "nccl"):
+        for mode in MODES:
             engine = TensorParallelEngine(gpu, batch=2, capacity=96, allreduce=mode)
             result[f"tp_logits_{mode}"] = oq.teacher_forced(engine, ids, 64).cpu()
             result[f"tokens_{mode}"], result[f"logprobs_{mode}"] = engine.generate(ids[:, :40], 12)
@@ -65,11 +68,12 @@ def test_tensor_parallel_engine_matches_the_single_gpu_engine(tmp_path):
     ref = r0["logits"]
     for r in (r0, r1):
         assert r["device_error"] == 0
-        for mode in ("nvlink", "nccl"):
+        for mode in MODES:
             assert ((r[f"tp_logits_{mode}"] - ref).abs() <= 4 * 2 ** -8 * ref.abs() + 0.05).all()
             assert torch.equal(r[f"tokens_{mode}"], r0[f"tokens_{mode}"])  # every rank samples the same tokens
         # two addends sum to the same bits in either order: the peer-memory all-reduce equals NCCL's
         assert torch.equal(r["tp_logits_nvlink"], r["tp_logits_nccl"])
-    agree = (r0["tokens_nvlink"] == r0["ref_tokens"]).float().mean()
-    assert agree > 0.9, (r0["tokens_nvlink"], r0["ref_tokens"])
-    assert torch.allclose(r0["logprobs_nvlink"][:, :1], r0["ref_logprobs"][:, :1], atol=0.05)
+    for mode in MODES:
+        agree = (r0[f"tokens_{mode}"] == r0["ref_tokens"]).float().mean()
+        assert agree > 0.9, (mode, r0[f"tokens_{mode}"], r0["ref_tokens"])
+        assert torch.allclose(r0[f"logprobs_{mode}"][:, :1], r0["ref_logprobs"][:, :1], atol=0.05)
