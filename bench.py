@@ -318,8 +318,8 @@ def run_ours(args, rank: int, world: int) -> dict | None:
 
 def run_tp(args, rank: int, world: int) -> dict | None:
     """The tensor-parallel latency case (B=1): the model split over `world` GPUs
-    (ipe_b200.tp.TensorParallelEngine, decode all-reduces over NVLink peer memory), decode tok/s of
-    the W1 generation, device time max over ranks."""
+    (ipe_b200.tp.TensorParallelEngine; by default the one-kernel step with the exchanges over NVLink
+    peer memory inside it), decode tok/s of the W1 generation, device time max over ranks."""
     import torch.distributed as dist
 
     from ipe_b200 import QWEN3_1_7B
@@ -445,7 +445,7 @@ def main() -> None:
     parser.add_argument("--new-tokens", type=int, default=0, help="override the workload's new tokens (profiling)")
     parser.add_argument("--layers", type=int, default=0, help="fewer decoder layers (profiling only; not a bench line)")
     parser.add_argument("--tp", action="store_true", help="tensor-parallel B=1 latency mode over the launched ranks")
-    parser.add_argument("--tp-allreduce", default="nvlink", choices=("nvlink", "nccl"))
+    parser.add_argument("--tp-allreduce", default="fused", choices=("fused", "nvlink", "nccl"))
     args = parser.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":

@@ -332,10 +332,11 @@ typedef struct {
    * intermediate and vocab (LM-head rows, from vocab_offset) are then this rank's shard; the
    * weights, caches and tiles above are the shard's. o_proj and down_proj push fp32 parts into
    * every rank's communication region (tp_peers: device array of the tp_world region pointers,
-   * ipe_decode_step_comm_bytes each, zero-filled once) and the next phase sums them, as does the
-   * sampler with every rank's LM-head records: every rank gets the same token. x_alt: a second
-   * bf16 [batch, hidden] residual buffer. Needs hidden % 256 == 0 and the activations in shared
-   * memory (batch <= 4 at Qwen3-1.7B). */
+   * ipe_decode_step_comm_bytes each, zero-filled once) as flagged 16-byte lines, and the next
+   * phase polls and sums them in rank order; the LM-head records go to every rank the same way
+   * and every rank samples the same token. No grid barrier follows a row-parallel phase. x_alt: a
+   * second bf16 [batch, hidden] residual buffer. Needs hidden % 512 == 0 and the activations in
+   * shared memory (the launch fails with a message when the batch is too large for that). */
   int tp_world, tp_rank;
   const void* tp_peers;
   void* x_alt;
@@ -344,13 +345,15 @@ typedef struct {
 } ipe_decode_step_desc;
 
 /* Step trace (when desc.trace is set): CTA c writes globaltimer nanoseconds to
- * trace[c * IPE_TRACE_WORDS(layers) + i]: i = 0 kernel start; for grid barrier j = 1 .. 5*layers+2
- * (embedding, then per layer after QKV, attention, o_proj, gate/up, down_proj, then the LM head),
- * i = 5j-4 its arrival, 5j-3 its release, and for the phase that follows it: 5j-2 activations
- * staged, 5j-1 first weight tile (attention: first item) ready, 5j last weight tile ready (last
- * item done); the last word the CTA's end. Words of events that did not happen are left as they
- * were. The array needs ipe_decode_step_grid() * IPE_TRACE_WORDS(layers) words. */
-#define IPE_TRACE_WORDS(layers) (25 * (layers) + 12)
+ * trace[c * IPE_TRACE_WORDS(layers) + i]: i = 0 kernel start; for phase end j = 1 .. 5*layers+2
+ * (embedding, then per layer after QKV, attention, o_proj, gate/up, down_proj, then the LM head;
+ * a grid barrier, except after o_proj, down_proj and the LM head of a tensor-parallel step),
+ * i = 5j-4 its arrival, 5j-3 its release (the same time without a barrier), and for the phase
+ * that follows it: 5j-2 activations staged, 5j-1 first weight tile (attention: first item) ready,
+ * 5j last weight tile ready (last item done); the second-to-last word the CTA's end of the LM
+ * head, the last its exit (CTA 0: after sampling). Words of events that did not happen are left
+ * as they were. The array needs ipe_decode_step_grid() * IPE_TRACE_WORDS(layers) words. */
+#define IPE_TRACE_WORDS(layers) (25 * (layers) + 13)
 int ipe_decode_step_grid(void);
 
 /* One whole decode step (embedding, all layers, final norm, LM head, and the sampler when

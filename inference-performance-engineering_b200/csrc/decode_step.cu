@@ -69,12 +69,13 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
   return v;
 }
 
-// Grid barrier among the consumer warps of all CTAs. Returns false when the step is aborted.
-// trace (this CTA's row of the step trace, or null) receives the arrival and release times.
-__device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort_smem, uint64_t* trace) {
+// Grid barrier among the consumer warps of all CTAs (the index-th of the step). Returns false when
+// the step is aborted. tr (this barrier's words in this CTA's row of the step trace, or null)
+// receives the arrival and release times.
+__device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort_smem, uint64_t* tr) {
   consumers_sync();
   if (tid == 0) {
-    if (trace) trace[1 + 5 * (index - 1)] = globaltimer_ns();
+    if (tr) tr[0] = globaltimer_ns();
     __threadfence();
     atomicAdd(&a.grid_bar[0], 1u);
     const unsigned target = index * gridDim.x;
@@ -98,80 +99,185 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
       __nanosleep(64);
     }
     __threadfence();
-    if (trace) trace[2 + 5 * (index - 1)] = globaltimer_ns();
+    if (tr) tr[1] = globaltimer_ns();
   }
   consumers_sync();
   return *abort_smem == 0;
 }
 
 // --------------------------------------------------------------------- tensor parallelism
-// Communication region of a rank (see ipe_decode_step_comm_bytes): u32 flag[r] at byte 4 r (the
-// last epoch rank r announced here), the epoch counter at byte 128, then the receive buffers.
-constexpr size_t kTpFlags = 0;
+// Communication region of a rank (ipe_decode_step_comm_bytes): the epoch counter at byte 128 (the
+// last exchange epoch of the previous step), then the receive buffers. Every value a peer sends is
+// a flagged line: 16 bytes {value, epoch, value, epoch} written by one 16-byte store, so a reader
+// that sees the current epoch in both flag words holds both values (the exchange needs no fence
+// and no barrier; each exchange has its own epoch, so a line from an earlier one never passes).
 constexpr size_t kTpCounter = 128;
 constexpr size_t kTpRecv = 256;
+constexpr size_t kTpLine = 16;
+constexpr size_t kTpRecordBytes = 3 * kTpLine;  // sampling record words 0..5: {m, s} {gs, gl} {arg, garg}
 
 __device__ __forceinline__ unsigned char* tp_region(const ipe_decode_step_desc& d, int r) {
   return reinterpret_cast<unsigned char*>(static_cast<const uint64_t*>(d.tp_peers)[r]);
 }
 
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_line(void* p, uint32_t w0, uint32_t w1, unsigned epoch) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w0), "r"(epoch), "r"(w1),
+               "r"(epoch)
+               : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_line(const void* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
   return v;
 }
 
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
+__device__ __forceinline__ bool line_ready(const uint4& v, unsigned epoch) { return v.y == epoch && v.w == epoch; }
 
-// A grid barrier that is also an exchange with the other ranks: every CTA makes its pushes to the
-// peers visible and arrives; CTA 0, once all have arrived, announces `epoch` to every peer and
-// waits (bounded) for every peer's announcement, then releases this GPU's CTAs. After it, every
-// rank's pushes of the phase are in this rank's receive buffers. epoch matters in CTA 0 only.
-__device__ bool grid_sync_tp(const StepArgs& a, unsigned index, int tid, int* abort_smem, unsigned epoch) {
-  consumers_sync();
-  if (tid == 0) {
-    const ipe_decode_step_desc& d = a.d;
-    __threadfence_system();
-    atomicAdd(&a.grid_bar[0], 1u);
-    bool ok = true;
-    uint64_t start = 0;
-    auto waiting = [&](unsigned i) {  // false once the step is aborted or the wait limit passed
-      __nanosleep(32);
-      if ((i & 63u) != 63u) return true;
-      if (ld_acquire(&a.grid_bar[1])) return false;
+// Re-reads the line at p until it carries `epoch` and returns it; once the step is aborted or the
+// wait limit passed (the error word is set and every CTA is told to leave), returns the last read,
+// which the caller sees is not ready.
+__device__ __noinline__ uint4 wait_line(const StepArgs& a, const void* p, unsigned epoch) {
+  uint64_t start = 0;
+  for (unsigned i = 0;; ++i) {
+    const uint4 v = ld_line(p);
+    if (line_ready(v, epoch)) return v;
+    if ((i & 63u) == 63u) {
+      if (ld_acquire(&a.grid_bar[1])) return v;
       const uint64_t now = globaltimer_ns();
       if (start == 0) start = now;
       else if (now - start > kWaitLimitNs) {
         report(a.err, kErrWaitTimeout);
         atomicExch(&a.grid_bar[1], 1u);
-        return false;
+        return v;
       }
-      return true;
-    };
-    if (blockIdx.x == 0) {
-      const unsigned target = index * gridDim.x;
-      for (unsigned i = 0; ok && ld_acquire(&a.grid_bar[0]) < target; ++i) ok = waiting(i);
-      if (ok) {
-        __threadfence_system();
-        for (int r = 0; r < d.tp_world; ++r)
-          if (r != d.tp_rank) st_release_sys(reinterpret_cast<unsigned*>(tp_region(d, r) + kTpFlags) + d.tp_rank, epoch);
-        const unsigned* flags = reinterpret_cast<const unsigned*>(tp_region(d, d.tp_rank) + kTpFlags);
-        for (int r = 0; r < d.tp_world && ok; ++r) {
-          if (r == d.tp_rank) continue;
-          for (unsigned i = 0; ok && static_cast<int>(ld_acquire_sys(flags + r) - epoch) < 0; ++i) ok = waiting(i);
+    }
+    __nanosleep(32);
+  }
+}
+
+// The staging of a tensor-parallel phase (see stage_tp in the kernel), kept out of line so that
+// its registers do not weigh on the weight-streaming loop.
+struct TpStage {
+  const bf16* x_old;
+  bf16* x_new;
+  const unsigned char* parts;  // this rank's receive slot (world parts), or null: x_old as is
+  const bf16* norm_w;          // nullable
+  bf16* xs;                    // shared [batch][hidden + kPad]
+  float* red_ss;               // shared [4 warps][16 rows]
+  size_t part_bytes;
+  unsigned epoch;
+  int* abort_smem;
+};
+
+__device__ __noinline__ void tp_stage(const StepArgs& a, const TpStage& st, int tid) {
+  const ipe_decode_step_desc& d = a.d;
+  const int B = d.batch, H = d.hidden, G_ = static_cast<int>(gridDim.x);
+  const int lane = tid & 31, cw = tid >> 5;
+  const int chunks = H / 16, total = B * chunks;
+  bool ok = true;
+  if (st.norm_w && lane == 0)
+    for (int b = 0; b < B; ++b) st.red_ss[cw * 16 + b] = 0.f;
+  for (int i = tid; i < total; i += kCThreads) {  // warp-uniform rows: chunks is a multiple of 32
+    const int b = i / chunks, k = i % chunks;
+    const bf16* xo = st.x_old + static_cast<int64_t>(b) * H + k * 16;
+    float f[16];
+    unpack8(ldcg16(xo), f);
+    unpack8(ldcg16(xo + 8), f + 8);
+    if (st.parts) {
+      float sum[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) sum[e] = 0.f;
+      for (int r = 0; r < d.tp_world; ++r) {
+        const unsigned char* lines = st.parts + r * st.part_bytes + (static_cast<size_t>(b) * chunks + k) * 8 * kTpLine;
+        uint4 v[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) v[q] = ld_line(lines + q * kTpLine);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (!line_ready(v[q], st.epoch) && ok) {
+            v[q] = wait_line(a, lines + q * kTpLine, st.epoch);
+            ok = line_ready(v[q], st.epoch);
+          }
+          sum[q] += __uint_as_float(v[q].x);
+          sum[q + 8] += __uint_as_float(v[q].z);
         }
       }
-      if (ok) asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(&a.grid_bar[2]), "r"(index) : "memory");
-    } else {
-      for (unsigned i = 0; ok && ld_acquire(&a.grid_bar[2]) < index; ++i) ok = waiting(i);
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = bf16_round(f[e] + bf16_round(sum[e]));
     }
-    if (!ok) *abort_smem = 1;
-    __threadfence();
+    const uint4 lo = pack8(f), hi = pack8(f + 8);
+    if (st.x_new && i % G_ == static_cast<int>(blockIdx.x)) {
+      bf16* xn = st.x_new + static_cast<int64_t>(b) * H + k * 16;
+      *reinterpret_cast<uint4*>(xn) = lo;
+      *reinterpret_cast<uint4*>(xn + 8) = hi;
+    }
+    *reinterpret_cast<uint4*>(st.xs + b * (H + kPad) + k * 16) = lo;
+    *reinterpret_cast<uint4*>(st.xs + b * (H + kPad) + k * 16 + 8) = hi;
+    if (st.norm_w) {
+      float sq = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) sq += f[e] * f[e];
+      sq = warp_sum(sq);
+      if (lane == 0) st.red_ss[cw * 16 + b] += sq;
+    }
+  }
+  if (!ok) *st.abort_smem = 1;
+  if (st.norm_w) {
+    consumers_sync();
+    const int chunks8 = H / 8;
+    for (int i = tid; i < B * chunks8; i += kCThreads) {
+      const int b = i / chunks8, c = i % chunks8;
+      const float* ss = st.red_ss;
+      const float r = rsqrtf((ss[b] + ss[16 + b] + ss[32 + b] + ss[48 + b]) / static_cast<float>(H) + d.eps);
+      float f[8], w[8];
+      unpack8(*reinterpret_cast<const uint4*>(st.xs + b * (H + kPad) + c * 8), f);
+      unpack8(ldg16(st.norm_w + c * 8), w);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = w[e] * bf16_round(f[e] * r);
+      *reinterpret_cast<uint4*>(st.xs + b * (H + kPad) + c * 8) = pack8(f);
+    }
   }
   consumers_sync();
-  return *abort_smem == 0;
+}
+
+// Row b's merge, over this lane's share (p = lane, lane + 32, ...) of `parts` flagged records at
+// recs, 4 records in flight. ok is cleared when a record does not arrive (the step is aborted).
+struct MergedRecords {
+  Stat st;
+  bool ok;
+};
+
+__device__ __noinline__ MergedRecords tp_merge_records(const StepArgs& a, const unsigned char* recs, int parts, int b,
+                                                       int lane, unsigned epoch) {
+  const int B = a.d.batch;
+  MergedRecords m{empty_stat(), true};
+  for (int p0 = lane; p0 < parts; p0 += 4 * 32) {
+    uint4 v[4][3];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int q = 0; q < 3; ++q)
+        if (p0 + 32 * k < parts)
+          v[k][q] = ld_line(recs + (static_cast<size_t>(p0 + 32 * k) * B + b) * kTpRecordBytes + q * kTpLine);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int p = p0 + 32 * k;
+      if (p >= parts) break;
+#pragma unroll
+      for (int q = 0; q < 3; ++q)
+        if (!line_ready(v[k][q], epoch) && m.ok) {
+          v[k][q] = wait_line(a, recs + (static_cast<size_t>(p) * B + b) * kTpRecordBytes + q * kTpLine, epoch);
+          m.ok = line_ready(v[k][q], epoch);
+        }
+      m.st = merge(m.st, Stat{__uint_as_float(v[k][0].x), __uint_as_float(v[k][0].z), static_cast<int>(v[k][2].x),
+                              __uint_as_float(v[k][1].x), static_cast<int>(v[k][2].z), __uint_as_float(v[k][1].z)});
+    }
+  }
+  return m;
 }
 
 // First unit of this CTA in a phase that starts dealing at `cursor`.
@@ -214,7 +320,9 @@ struct UnitWalk {
   PhaseShape ph{};
 };
 
-template <int NT, int G, bool ACT_SMEM>
+// TP: a tensor-parallel rank (tp_world > 1; needs ACT_SMEM), compiled apart so that the one-GPU
+// variants carry none of its code.
+template <int NT, int G, bool ACT_SMEM, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   const int S = a.slots;
@@ -374,7 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   const int g = lane >> 2, t = lane & 3;
   SlotCursor mine;
   int cursor = 0;
-  unsigned barrier_index = 0;
+  // phase ends so far (each a grid barrier, or in tensor-parallel steps after a row-parallel phase
+  // the end of this CTA's pushes), and grid barriers so far
+  unsigned barrier_index = 0, syncs = 0;
   int64_t* state = d.state;
   uint64_t* trace = d.trace ? d.trace + static_cast<int64_t>(blockIdx.x) * IPE_TRACE_WORDS(d.layers) : nullptr;
   if (trace && tid == 0) trace[0] = globaltimer_ns();
@@ -382,12 +492,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   auto mark = [&](int k) {
     if (trace && tid == 0) trace[1 + 5 * (barrier_index - 1) + k] = globaltimer_ns();
   };
-  // tensor parallelism: this rank's region, and the epoch of its exchanges (CTA 0, thread 0)
-  const bool tp = d.tp_world > 1;
+  // the end of a phase: a grid barrier, or (tensor parallel, after a row-parallel phase) none: the
+  // readers of the pushed parts poll them
+  auto phase_end = [&](bool barrier) -> bool {
+    ++barrier_index;
+    uint64_t* tr = trace ? trace + 1 + 5 * (barrier_index - 1) : nullptr;
+    if (barrier) return grid_sync(a, ++syncs, tid, abort_smem, tr);
+    if (tr && tid == 0) tr[0] = tr[1] = globaltimer_ns();
+    return true;
+  };
+  // tensor parallelism: this rank's region and the epoch of the current exchange. Every CTA reads
+  // the counter before the first grid barrier; CTA 0 advances it at the end of the step.
+  constexpr bool tp = TP;
   unsigned char* my_region = tp ? tp_region(d, d.tp_rank) : nullptr;
-  unsigned tp_epoch = (tp && blockIdx.x == 0 && tid == 0) ? *reinterpret_cast<const unsigned*>(my_region + kTpCounter) : 0u;
-  const size_t x_part_bytes = static_cast<size_t>(B) * H * sizeof(float);
-  const size_t rec_rank_bytes = static_cast<size_t>(a.parts_max) * B * IPE_PARTIAL_WORDS * sizeof(float);
+  unsigned tp_epoch = tp ? *reinterpret_cast<const volatile unsigned*>(my_region + kTpCounter) : 0u;
+  const size_t x_part_bytes = static_cast<size_t>(B) * H / 2 * kTpLine;  // one rank's part: 2 values a line
+  const size_t rec_rank_bytes = static_cast<size_t>(a.parts_max) * B * kTpRecordBytes;
   __shared__ float red_ss[4 * 16];  // tensor-parallel staging: [warp][row] sums of squares
   int tp_slot = 0;                  // receive slot of the current row-parallel phase
 
@@ -405,7 +525,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       *reinterpret_cast<uint4*>(x + static_cast<int64_t>(b) * H + v * 8) = val;
     }
   }
-  if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
+  if (!phase_end(true)) return;
 
   // Stage the activation rows of a phase (optionally RMS-normalised) in shared memory; without
   // shared staging only the RMS scales are kept and tiles read activations from global memory.
@@ -416,90 +536,56 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   };
 
   // (tensor parallel) The residual stream after a row-parallel layer, x = bf16(x_old + bf16(sum
-  // over the ranks, in rank order, of the parts in receive slot `slot`)) (slot < 0: x_old as is),
-  // staged in shared memory, RMS-normalised with norm_w when non-null; chunk i of it also goes to
-  // x_new (when non-null) from CTA i % grid, so the next residual base is whole after the next
-  // barrier. Every CTA runs it, with or without units. Needs hidden % 256 == 0.
-  auto stage_tp = [&](const bf16* x_old, bf16* x_new, int slot, const bf16* norm_w) {
-    const int chunks = H / 8, total = B * chunks;
-    const float* parts = slot >= 0 ? reinterpret_cast<const float*>(my_region + a.recv_x + slot * d.tp_world * x_part_bytes)
-                                   : nullptr;
-    if (norm_w && lane == 0)
-      for (int b = 0; b < B; ++b) red_ss[cw * 16 + b] = 0.f;
-    for (int i = tid; i < total; i += kCThreads) {  // warp-uniform rows: chunks is a multiple of 32
-      const int b = i / chunks, c = i % chunks;
-      float f[8];
-      unpack8(ldcg16(x_old + static_cast<int64_t>(b) * H + c * 8), f);
-      if (parts) {
-        float sum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int r = 0; r < d.tp_world; ++r) {
-          const float4* q = reinterpret_cast<const float4*>(parts + (static_cast<int64_t>(r) * B + b) * H + c * 8);
-          const float4 lo = __ldcv(q), hi = __ldcv(q + 1);  // pushed by the peers: read fresh
-          sum[0] += lo.x; sum[1] += lo.y; sum[2] += lo.z; sum[3] += lo.w;
-          sum[4] += hi.x; sum[5] += hi.y; sum[6] += hi.z; sum[7] += hi.w;
-        }
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = bf16_round(f[e] + bf16_round(sum[e]));
-      }
-      const uint4 packed = pack8(f);
-      if (x_new && i % G_ == static_cast<int>(blockIdx.x))
-        *reinterpret_cast<uint4*>(x_new + static_cast<int64_t>(b) * H + c * 8) = packed;
-      *reinterpret_cast<uint4*>(xs + b * (H + kPad) + c * 8) = packed;
-      if (norm_w) {
-        float sq = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) sq += f[e] * f[e];
-        sq = warp_sum(sq);
-        if (lane == 0) red_ss[cw * 16 + b] += sq;
-      }
-    }
-    if (norm_w) {
-      consumers_sync();
-      for (int i = tid; i < total; i += kCThreads) {
-        const int b = i / chunks, c = i % chunks;
-        const float r = rsqrtf((red_ss[b] + red_ss[16 + b] + red_ss[32 + b] + red_ss[48 + b]) / static_cast<float>(H) +
-                               d.eps);
-        float f[8], w[8];
-        unpack8(*reinterpret_cast<const uint4*>(xs + b * (H + kPad) + c * 8), f);
-        unpack8(ldg16(norm_w + c * 8), w);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = w[e] * bf16_round(f[e] * r);
-        *reinterpret_cast<uint4*>(xs + b * (H + kPad) + c * 8) = pack8(f);
-      }
-    }
-    consumers_sync();
+  // over the ranks, in rank order, of their parts in receive slot `slot`)) (slot < 0: x_old as
+  // is), staged in shared memory, RMS-normalised with norm_w when non-null; 16-column chunk i of it
+  // also goes to x_new (when non-null) from CTA i % grid, so the next residual base is whole after
+  // the next grid barrier. The parts are polled line by line (epoch tp_epoch). Every CTA runs it,
+  // with or without units. Needs hidden % 512 == 0. false when the step is aborted.
+  //
+  // A part is [batch][hidden / 16][8 lines]: line q of 16-column group k of row b holds columns
+  // 16 k + q and 16 k + q + 8 (the pair one lane of the row-block epilogue owns).
+  auto stage_tp = [&](const bf16* x_old, bf16* x_new, int slot, const bf16* norm_w) -> bool {
+    TpStage st{x_old,     x_new, slot >= 0 ? my_region + a.recv_x + static_cast<size_t>(slot) * d.tp_world * x_part_bytes
+                                           : nullptr,
+               norm_w,    xs,    red_ss,
+               x_part_bytes, tp_epoch, abort_smem};
+    tp_stage(a, st, tid);
     mark(2);
+    return *abort_smem == 0;
   };
 
-  // (tensor parallel) A row-parallel unit's fp32 sums into every rank's receive slot tp_slot.
+  // (tensor parallel) A row-parallel unit's fp32 sums, as flagged lines, into every rank's receive
+  // slot tp_slot (this rank's part).
   auto push_parts = [&](const float (&acc)[2][NT][4], int rb, int first_half, int halves) {
+    const int chunks = H / 16;
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       if (h >= halves) break;
 #pragma unroll
       for (int j = 0; j < NT; ++j)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int n = rb * 32 + (first_half + h) * 16 + g + 8 * (e >> 1);
-          const int b = 8 * j + 2 * t + (e & 1);
-          if (b >= B || n >= H) continue;
-          for (int r = 0; r < d.tp_world; ++r) {
-            float* dst = reinterpret_cast<float*>(tp_region(d, r) + a.recv_x +
-                                                  (static_cast<size_t>(tp_slot) * d.tp_world + d.tp_rank) * x_part_bytes);
-            dst[b * H + n] = acc[h][j][e];
-          }
+        for (int e = 0; e < 2; ++e) {
+          const int b = 8 * j + 2 * t + e;
+          if (b >= B) continue;
+          const size_t off = a.recv_x + (static_cast<size_t>(tp_slot) * d.tp_world + d.tp_rank) * x_part_bytes +
+                             ((static_cast<size_t>(b) * chunks + rb * 2 + first_half + h) * 8 + g) * kTpLine;
+          for (int r = 0; r < d.tp_world; ++r)
+            st_line(tp_region(d, r) + off, __float_as_uint(acc[h][j][e]), __float_as_uint(acc[h][j][e + 2]), tp_epoch);
         }
     }
   };
 
-  // (tensor parallel) The LM-head records of row block rb into every rank's record buffer.
+  // (tensor parallel) The sampling records of LM-head row block rb, as flagged lines, into every
+  // rank's record buffer.
   auto push_records = [&](int rb) {
     __syncwarp();
-    for (int l = lane; l < B * IPE_PARTIAL_WORDS; l += 32) {
-      const int64_t index = static_cast<int64_t>(rb) * B * IPE_PARTIAL_WORDS + l;
-      const float v = d.partials[index];
-      for (int r = 0; r < d.tp_world; ++r)
-        reinterpret_cast<float*>(tp_region(d, r) + a.recv_rec + d.tp_rank * rec_rank_bytes)[index] = v;
+    for (int l = lane; l < B * 3; l += 32) {
+      const int b = l / 3, q = l % 3;
+      const float* rec = d.partials + (static_cast<int64_t>(rb) * B + b) * IPE_PARTIAL_WORDS;
+      const uint32_t w0 = __float_as_uint(rec[2 * q]), w1 = __float_as_uint(rec[2 * q + 1]);
+      const size_t off = a.recv_rec + d.tp_rank * rec_rank_bytes + (static_cast<size_t>(rb) * B + b) * kTpRecordBytes +
+                         q * kTpLine;
+      for (int r = 0; r < d.tp_world; ++r) st_line(tp_region(d, r) + off, w0, w1, tp_epoch);
     }
   };
 
@@ -623,12 +709,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     const ipe_layer_desc& L = d.layer_descs[layer];
     // QKV projection (input RMSNorm fused); tensor parallel: after the previous layer's down_proj
     // parts, the residual stream moves from x to x_alt
-    if (tp) stage_tp(x, static_cast<bf16*>(d.x_alt), layer == 0 ? -1 : 1, static_cast<const bf16*>(L.input_layernorm));
-    else stage(x, static_cast<const bf16*>(L.input_layernorm), H);
+    if (tp) {
+      if (!stage_tp(x, static_cast<bf16*>(d.x_alt), layer == 0 ? -1 : 1, static_cast<const bf16*>(L.input_layernorm)))
+        return;
+    } else {
+      stage(x, static_cast<const bf16*>(L.input_layernorm), H);
+    }
     if (!run_phase(EpiStore{}, phase_shape(layer, 0), x, static_cast<const bf16*>(L.input_layernorm), H,
                    EpilogueArgs{qkv, QKV, QKV, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
+    if (!phase_end(true)) return;
     // attention: items (split, KV head, row) over the CTAs
     {
       FusedArgs fa{};
@@ -658,49 +748,52 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
         mark(4);
       }
     }
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
+    if (!phase_end(true)) return;
     // o_proj + residual (tensor parallel: this rank's part, pushed to every rank)
     stage(attn, nullptr, Q);
     tp_slot = 0;
+    ++tp_epoch;
     if (!run_phase(EpiResidual{}, phase_shape(layer, 1), attn, nullptr, Q,
                    EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!(tp ? grid_sync_tp(a, ++barrier_index, tid, abort_smem, ++tp_epoch)
-             : grid_sync(a, ++barrier_index, tid, abort_smem, trace)))
-      return;
+    if (!phase_end(!tp)) return;
     // post-attention RMSNorm + gate/up + SiLU * up (tensor parallel: the residual stream moves back
     // from x_alt to x with the o_proj parts)
-    if (tp) stage_tp(static_cast<const bf16*>(d.x_alt), x, 0, static_cast<const bf16*>(L.post_attention_layernorm));
-    else stage(x, static_cast<const bf16*>(L.post_attention_layernorm), H);
+    if (tp) {
+      if (!stage_tp(static_cast<const bf16*>(d.x_alt), x, 0, static_cast<const bf16*>(L.post_attention_layernorm)))
+        return;
+    } else {
+      stage(x, static_cast<const bf16*>(L.post_attention_layernorm), H);
+    }
     if (!run_phase(EpiSilu{}, phase_shape(layer, 2), x, static_cast<const bf16*>(L.post_attention_layernorm), H,
                    EpilogueArgs{act, I, 2 * I, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!grid_sync(a, ++barrier_index, tid, abort_smem, trace)) return;
+    if (!phase_end(true)) return;
     // down_proj + residual (tensor parallel: this rank's part, pushed to every rank)
     stage(act, nullptr, I);
     tp_slot = 1;
+    ++tp_epoch;
     if (!run_phase(EpiResidual{}, phase_shape(layer, 3), act, nullptr, I,
                    EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
       return;
-    if (!(tp ? grid_sync_tp(a, ++barrier_index, tid, abort_smem, ++tp_epoch)
-             : grid_sync(a, ++barrier_index, tid, abort_smem, trace)))
-      return;
+    if (!phase_end(!tp)) return;
   }
   // final RMSNorm + tied LM head: fp32 logits and one sampling record per 32 vocabulary rows
   // (tensor parallel: this rank's vocabulary rows, records pushed to every rank)
   if (tp) {
-    stage_tp(x, nullptr, 1, static_cast<const bf16*>(d.final_norm));
+    if (!stage_tp(x, nullptr, 1, static_cast<const bf16*>(d.final_norm))) return;
+    ++tp_epoch;
     // neutral records for this rank's padding up to the largest shard's record count
     const int parts_mine = (d.vocab + 31) / 32;
-    for (int l = tid; l < (a.parts_max - parts_mine) * B; l += kCThreads) {
-      if (blockIdx.x != 0) break;
-      const int64_t index = (static_cast<int64_t>(parts_mine) * B + l) * IPE_PARTIAL_WORDS;
-      const float rec[IPE_PARTIAL_WORDS] = {-INFINITY, 0.f, -INFINITY, 0.f, __int_as_float(0x7fffffff),
-                                            __int_as_float(0x7fffffff), 0.f, 0.f};
-      for (int r = 0; r < d.tp_world; ++r)
-        for (int w = 0; w < IPE_PARTIAL_WORDS; ++w)
-          reinterpret_cast<float*>(tp_region(d, r) + a.recv_rec + d.tp_rank * rec_rank_bytes)[index + w] = rec[w];
-    }
+    if (blockIdx.x == 0)
+      for (int l = tid; l < (a.parts_max - parts_mine) * B * 3; l += kCThreads) {
+        const int q = l % 3;
+        const uint32_t w0 = q == 2 ? 0x7fffffffu : __float_as_uint(-INFINITY);  // {m, s} {gs, gl} {arg, garg}
+        const uint32_t w1 = q == 2 ? 0x7fffffffu : 0u;
+        const size_t off = a.recv_rec + d.tp_rank * rec_rank_bytes +
+                           (static_cast<size_t>(parts_mine) * B + l / 3) * kTpRecordBytes + q * kTpLine;
+        for (int r = 0; r < d.tp_world; ++r) st_line(tp_region(d, r) + off, w0, w1, tp_epoch);
+      }
   } else {
     stage(x, static_cast<const bf16*>(d.final_norm), H);
   }
@@ -709,33 +802,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     ea.row_offset = d.vocab_offset;
     if (!run_phase(EpiLogits{}, phase_shape(d.layers, 0), x, static_cast<const bf16*>(d.final_norm), H, ea)) return;
   }
-  if (!(tp ? grid_sync_tp(a, ++barrier_index, tid, abort_smem, ++tp_epoch)
-           : grid_sync(a, ++barrier_index, tid, abort_smem, trace)))
-    return;
-  if (trace && tid == 0) trace[IPE_TRACE_WORDS(d.layers) - 1] = globaltimer_ns();
+  // Tensor parallel: no barrier; CTA 0 polls every rank's records, each pushed after its epilogue
+  // read the step state, so the state may change once they are all in.
+  if (!phase_end(!tp)) return;
+  if (trace && tid == 0) trace[IPE_TRACE_WORDS(d.layers) - 2] = globaltimer_ns();
   if (blockIdx.x != 0) return;
 
   // Sampling (CTA 0): token and untempered log-probability per row, fed back as the next input.
   // Tensor parallel: over every rank's records (the same on every rank); the chosen token's logit
   // then comes from the records.
   const int parts = tp ? d.tp_world * a.parts_max : (d.vocab + 31) / 32;
-  const float* records = tp ? reinterpret_cast<const float*>(my_region + a.recv_rec) : d.partials;
+  bool ok = true;
   if (d.history_tokens) {
     const float temperature = __int_as_float(static_cast<int>(state[IPE_STATE_TEMPERATURE]));
     const int64_t step = state[IPE_STATE_STEP];
     for (int b = cw; b < B; b += kConsumers) {
       Stat st = empty_stat();
-      for (int p = lane; p < parts; p += 32)
-        st = merge(st, tp ? Stat{__ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS),
-                                 __ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 1),
-                                 __float_as_int(__ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 4)),
-                                 __ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 2),
-                                 __float_as_int(__ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 5)),
-                                 __ldcv(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS + 3)}
-                          : load_stat(records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
+      if (tp) {
+        const MergedRecords m = tp_merge_records(a, my_region + a.recv_rec, parts, b, lane, tp_epoch);
+        st = m.st;
+        ok = ok && m.ok;
+      } else {
+        for (int p = lane; p < parts; p += 32)
+          st = merge(st, load_stat(d.partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) st = merge(st, shfl_xor_stat(st, o));
-      if (lane == 0) {
+      if (lane == 0 && ok) {
         const int token = temperature > 0.f ? st.garg : st.arg;
         const float logit = tp ? (temperature > 0.f ? st.gl : st.m)
                                : __ldcg(d.logits + static_cast<int64_t>(b) * d.vocab + token);
@@ -745,18 +838,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       }
     }
   }
+  if (!ok) *abort_smem = 1;
   consumers_sync();
-  if (tid == 0) {
+  if (tid == 0 && *abort_smem == 0) {
     if (d.history_tokens) state[IPE_STATE_STEP] += 1;
     state[IPE_STATE_POS] = pos + 1;
-    if (tp) *reinterpret_cast<unsigned*>(my_region + kTpCounter) = tp_epoch;  // the exchanges of the next step
+    if (tp) *reinterpret_cast<unsigned*>(my_region + kTpCounter) = tp_epoch;  // the next step's epochs follow
   }
+  if (trace && tid == 0) trace[IPE_TRACE_WORDS(d.layers) - 1] = globaltimer_ns();
 }
 
 
-template <int NT, int G, bool ACT>
+template <int NT, int G, bool ACT, bool TP>
 cudaError_t launch_variant(const StepArgs& a, size_t smem, cudaStream_t stream) {
-  auto kernel = decode_step_kernel<NT, G, ACT>;
+  auto kernel = decode_step_kernel<NT, G, ACT, TP>;
   static bool configured = false;
   if (!configured) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -777,13 +872,13 @@ cudaError_t launch_variant(const StepArgs& a, size_t smem, cudaStream_t stream) 
   return cudaLaunchKernelEx(&config, kernel, a);
 }
 
-template <int NT, bool ACT>
+template <int NT, bool ACT, bool TP>
 cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
   switch (a.d.q_heads / a.d.kv_heads) {
-    case 1: return launch_variant<NT, 1, ACT>(a, smem, stream);
-    case 2: return launch_variant<NT, 2, ACT>(a, smem, stream);
-    case 4: return launch_variant<NT, 4, ACT>(a, smem, stream);
-    case 8: return launch_variant<NT, 8, ACT>(a, smem, stream);
+    case 1: return launch_variant<NT, 1, ACT, TP>(a, smem, stream);
+    case 2: return launch_variant<NT, 2, ACT, TP>(a, smem, stream);
+    case 4: return launch_variant<NT, 4, ACT, TP>(a, smem, stream);
+    case 8: return launch_variant<NT, 8, ACT, TP>(a, smem, stream);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -828,10 +923,14 @@ size_t attn_bytes(int group) {
 
 }  // namespace
 
+// Receive slots of the row-parallel parts: 2 slots x world parts x batch x hidden / 2 lines.
+size_t tp_parts_bytes(int world, int batch, int hidden) {
+  return (2ull * world * batch * (hidden / 2) * kTpLine + 255) / 256 * 256;
+}
+
 size_t decode_step_comm_bytes(int world, int batch, int hidden, int vocab_rows_max) {
   const size_t parts_max = (static_cast<size_t>(vocab_rows_max) + 31) / 32;
-  const size_t recv_x = (2ull * world * batch * hidden * sizeof(float) + 255) / 256 * 256;
-  return 256 + recv_x + static_cast<size_t>(world) * parts_max * batch * IPE_PARTIAL_WORDS * sizeof(float);
+  return kTpRecv + tp_parts_bytes(world, batch, hidden) + static_cast<size_t>(world) * parts_max * batch * kTpRecordBytes;
 }
 
 size_t decode_step_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity) {
@@ -870,20 +969,21 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
     return cudaErrorInvalidValue;
   }
   if (d.tp_world > 1) {
-    if (!act_smem || d.hidden % 256) {
-      *message = "tensor parallel: needs hidden % 256 == 0 and the activations in shared memory (a smaller batch)";
+    if (!act_smem || d.hidden % 512) {
+      *message = "tensor parallel: needs hidden % 512 == 0 and the activations in shared memory (a smaller batch)";
       return cudaErrorInvalidValue;
     }
     const int blocks = (d.vocab_total + 31) / 32;
     a.parts_max = (blocks + d.tp_world - 1) / d.tp_world;
-    a.recv_x = 256;
-    a.recv_rec = a.recv_x + (2ull * d.tp_world * d.batch * d.hidden * sizeof(float) + 255) / 256 * 256;
+    a.recv_x = kTpRecv;
+    a.recv_rec = a.recv_x + tp_parts_bytes(d.tp_world, d.batch, d.hidden);
   }
-  // the grid barrier counts arrivals from zero every step ([0] arrivals, [1] abort, [2] release)
-  cudaError_t e = cudaMemsetAsync(a.grid_bar, 0, 4 * sizeof(unsigned), stream);
+  // the grid barrier counts arrivals from zero every step ([0] arrivals, [1] abort)
+  cudaError_t e = cudaMemsetAsync(a.grid_bar, 0, 2 * sizeof(unsigned), stream);
   if (e != cudaSuccess) return e;
-  if (nt == 1) return act_smem ? by_group<1, true>(a, smem, stream) : by_group<1, false>(a, smem, stream);
-  return act_smem ? by_group<2, true>(a, smem, stream) : by_group<2, false>(a, smem, stream);
+  if (d.tp_world > 1) return nt == 1 ? by_group<1, true, true>(a, smem, stream) : by_group<2, true, true>(a, smem, stream);
+  if (nt == 1) return act_smem ? by_group<1, true, false>(a, smem, stream) : by_group<1, false, false>(a, smem, stream);
+  return act_smem ? by_group<2, true, false>(a, smem, stream) : by_group<2, false, false>(a, smem, stream);
 }
 
 }  // namespace ipe

@@ -98,7 +98,7 @@ class StepDesc(ctypes.Structure):
 
 def trace_words(layers: int) -> int:
     """IPE_TRACE_WORDS of include/ipe_b200.h: timestamps per CTA of one traced decode step."""
-    return 25 * layers + 12
+    return 25 * layers + 13
 
 
 class NativeUnavailable(RuntimeError):
