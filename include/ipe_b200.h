@@ -333,8 +333,8 @@ typedef struct {
    * weights, caches and tiles above are the shard's. o_proj and down_proj push fp32 parts into
    * every rank's communication region (tp_peers: device array of the tp_world region pointers,
    * ipe_decode_step_comm_bytes each, zero-filled once) as flagged 16-byte lines, and the next
-   * phase polls and sums them in rank order; the LM-head records go to every rank the same way
-   * and every rank samples the same token. No grid barrier follows a row-parallel phase. x_alt: a
+   * phase polls and sums them in rank order; each CTA's merge of its LM-head records goes to
+   * every rank the same way and every rank samples the same token. No grid barrier follows a row-parallel phase. x_alt: a
    * second bf16 [batch, hidden] residual buffer. Needs hidden % 512 == 0 and the activations in
    * shared memory (the launch fails with a message when the batch is too large for that). */
   int tp_world, tp_rank;
@@ -364,8 +364,10 @@ int ipe_decode_step_grid(void);
  * src/ipe/engine.py:84-111 (decode -> _step) and, with sampling, one iteration of
  * src/ipe/engine.py:137-147. */
 int ipe_decode_step(const ipe_decode_step_desc* desc, void* stream);
-/* Bytes of one rank's communication region for a tensor-parallel decode step. */
-size_t ipe_decode_step_comm_bytes(int tp_world, int batch, int hidden, int vocab_rows_max);
+/* Bytes of one rank's communication region for a tensor-parallel decode step on this device: the
+ * epoch counter, two receive slots of every rank's row-parallel part, and every rank's per-CTA
+ * merged LM-head records (0 for bad arguments). */
+size_t ipe_decode_step_comm_bytes(int tp_world, int batch, int hidden);
 size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capacity);
 
 /* ------------------------------------------------------------------ step state */

@@ -484,9 +484,9 @@ size_t ipe_decode_step_workspace(int batch, int q_heads, int kv_heads, int capac
 
 int ipe_decode_step_grid(void) { return ipe::sm_count(); }
 
-size_t ipe_decode_step_comm_bytes(int tp_world, int batch, int hidden, int vocab_rows_max) {
-  if (tp_world < 1 || batch < 1 || hidden < 1 || vocab_rows_max < 1) return 0;
-  return ipe::decode_step_comm_bytes(tp_world, batch, hidden, vocab_rows_max);
+size_t ipe_decode_step_comm_bytes(int tp_world, int batch, int hidden) {
+  if (tp_world < 1 || batch < 1 || hidden < 1) return 0;
+  return ipe::decode_step_comm_bytes(tp_world, batch, hidden);
 }
 
 int ipe_decode_step(const ipe_decode_step_desc* d, void* stream) {

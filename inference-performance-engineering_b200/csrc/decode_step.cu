@@ -53,10 +53,10 @@ struct StepArgs {
   unsigned prefetch_bytes;  // how far the L2 prefetch runs ahead of the shared-memory copies
   int evict_first;          // weight copies mark their L2 lines evict-first
   int halves;               // half-row-block units allowed
+  float* cta_records;       // [grid][batch][IPE_PARTIAL_WORDS]: each CTA's merge of its LM-head records
   // tensor parallelism (d.tp_world > 1): byte offsets in a communication region
-  size_t recv_x;            // [2 slots][world][batch][hidden] fp32 parts of o_proj / down_proj
-  size_t recv_rec;          // [world][parts_max][batch][IPE_PARTIAL_WORDS] LM-head records
-  int parts_max;            // LM-head records per rank (the largest shard's)
+  size_t recv_x;            // [2 slots][world][batch][hidden / 16][8 lines] parts of o_proj / down_proj
+  size_t recv_rec;          // [world][grid][batch][3 lines] the CTAs' merged LM-head records
 };
 
 __device__ __forceinline__ void consumers_sync() {
@@ -507,7 +507,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   unsigned char* my_region = tp ? tp_region(d, d.tp_rank) : nullptr;
   unsigned tp_epoch = tp ? *reinterpret_cast<const volatile unsigned*>(my_region + kTpCounter) : 0u;
   const size_t x_part_bytes = static_cast<size_t>(B) * H / 2 * kTpLine;  // one rank's part: 2 values a line
-  const size_t rec_rank_bytes = static_cast<size_t>(a.parts_max) * B * kTpRecordBytes;
   __shared__ float red_ss[4 * 16];  // tensor-parallel staging: [warp][row] sums of squares
   int tp_slot = 0;                  // receive slot of the current row-parallel phase
 
@@ -572,20 +571,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
           for (int r = 0; r < d.tp_world; ++r)
             st_line(tp_region(d, r) + off, __float_as_uint(acc[h][j][e]), __float_as_uint(acc[h][j][e + 2]), tp_epoch);
         }
-    }
-  };
-
-  // (tensor parallel) The sampling records of LM-head row block rb, as flagged lines, into every
-  // rank's record buffer.
-  auto push_records = [&](int rb) {
-    __syncwarp();
-    for (int l = lane; l < B * 3; l += 32) {
-      const int b = l / 3, q = l % 3;
-      const float* rec = d.partials + (static_cast<int64_t>(rb) * B + b) * IPE_PARTIAL_WORDS;
-      const uint32_t w0 = __float_as_uint(rec[2 * q]), w1 = __float_as_uint(rec[2 * q + 1]);
-      const size_t off = a.recv_rec + d.tp_rank * rec_rank_bytes + (static_cast<size_t>(rb) * B + b) * kTpRecordBytes +
-                         q * kTpLine;
-      for (int r = 0; r < d.tp_world; ++r) st_line(tp_region(d, r) + off, w0, w1, tp_epoch);
     }
   };
 
@@ -679,7 +664,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
             row_block_epilogue<EPI, NT>(acc, u >> 1, lane, ea, u & 1, 1);
         } else {
           row_block_epilogue<EPI, NT>(acc, u, lane, ea);
-          if (EPI == kGemvLogits && tp) push_records(u);
         }
       }
       consumers_sync();
@@ -778,32 +762,51 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       return;
     if (!phase_end(!tp)) return;
   }
-  // final RMSNorm + tied LM head: fp32 logits and one sampling record per 32 vocabulary rows
-  // (tensor parallel: this rank's vocabulary rows, records pushed to every rank)
+  // final RMSNorm + tied LM head: fp32 logits and one sampling record per 32 vocabulary rows, then
+  // one record per row merging this CTA's (tensor parallel: this rank's vocabulary rows, and the
+  // merged records go to every rank)
   if (tp) {
     if (!stage_tp(x, nullptr, 1, static_cast<const bf16*>(d.final_norm))) return;
     ++tp_epoch;
-    // neutral records for this rank's padding up to the largest shard's record count
-    const int parts_mine = (d.vocab + 31) / 32;
-    if (blockIdx.x == 0)
-      for (int l = tid; l < (a.parts_max - parts_mine) * B * 3; l += kCThreads) {
-        const int q = l % 3;
-        const uint32_t w0 = q == 2 ? 0x7fffffffu : __float_as_uint(-INFINITY);  // {m, s} {gs, gl} {arg, garg}
-        const uint32_t w1 = q == 2 ? 0x7fffffffu : 0u;
-        const size_t off = a.recv_rec + d.tp_rank * rec_rank_bytes +
-                           (static_cast<size_t>(parts_mine) * B + l / 3) * kTpRecordBytes + q * kTpLine;
-        for (int r = 0; r < d.tp_world; ++r) st_line(tp_region(d, r) + off, w0, w1, tp_epoch);
-      }
   } else {
     stage(x, static_cast<const bf16*>(d.final_norm), H);
   }
   {
+    const PhaseShape lm = phase_shape(d.layers, 0);
+    const int lm_first = first_unit(cursor);
     EpilogueArgs ea{d.logits, d.vocab, d.vocab, B, d.partials, state, 0.f, 0};
     ea.row_offset = d.vocab_offset;
-    if (!run_phase(EpiLogits{}, phase_shape(d.layers, 0), x, static_cast<const bf16*>(d.final_norm), H, ea)) return;
+    if (!run_phase(EpiLogits{}, lm, x, static_cast<const bf16*>(d.final_norm), H, ea)) return;
+    // rows over the consumer warps; this CTA's units lane-strided, then the lanes in a fixed tree
+    for (int b = cw; b < B; b += kConsumers) {
+      Stat st = empty_stat();
+      for (int u = lm_first + lane * G_; u < lm.units; u += 32 * G_)
+        st = merge(st, load_stat(d.partials + (static_cast<int64_t>(u) * B + b) * IPE_PARTIAL_WORDS));
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) st = merge(st, shfl_xor_stat(st, o));
+      if (lane == 0) {
+        if (tp) {
+          const size_t off = a.recv_rec + ((static_cast<size_t>(d.tp_rank) * G_ + blockIdx.x) * B + b) * kTpRecordBytes;
+          for (int r = 0; r < d.tp_world; ++r) {
+            unsigned char* dst = tp_region(d, r) + off;
+            st_line(dst, __float_as_uint(st.m), __float_as_uint(st.s), tp_epoch);
+            st_line(dst + kTpLine, __float_as_uint(st.gs), __float_as_uint(st.gl), tp_epoch);
+            st_line(dst + 2 * kTpLine, static_cast<uint32_t>(st.arg), static_cast<uint32_t>(st.garg), tp_epoch);
+          }
+        } else {
+          float* rec = a.cta_records + (static_cast<int64_t>(blockIdx.x) * B + b) * IPE_PARTIAL_WORDS;
+          rec[0] = st.m;
+          rec[1] = st.s;
+          rec[2] = st.gs;
+          rec[3] = st.gl;
+          rec[4] = __int_as_float(st.arg);
+          rec[5] = __int_as_float(st.garg);
+        }
+      }
+    }
   }
-  // Tensor parallel: no barrier; CTA 0 polls every rank's records, each pushed after its epilogue
-  // read the step state, so the state may change once they are all in.
+  // Tensor parallel: no barrier; CTA 0 polls every rank's records, each pushed after its
+  // epilogues read the step state, so the state may change once they are all in.
   if (!phase_end(!tp)) return;
   if (trace && tid == 0) trace[IPE_TRACE_WORDS(d.layers) - 2] = globaltimer_ns();
   if (blockIdx.x != 0) return;
@@ -811,7 +814,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   // Sampling (CTA 0): token and untempered log-probability per row, fed back as the next input.
   // Tensor parallel: over every rank's records (the same on every rank); the chosen token's logit
   // then comes from the records.
-  const int parts = tp ? d.tp_world * a.parts_max : (d.vocab + 31) / 32;
+  const int parts = tp ? d.tp_world * G_ : G_;  // the CTAs' merged records
   bool ok = true;
   if (d.history_tokens) {
     const float temperature = __int_as_float(static_cast<int>(state[IPE_STATE_TEMPERATURE]));
@@ -824,7 +827,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
         ok = ok && m.ok;
       } else {
         for (int p = lane; p < parts; p += 32)
-          st = merge(st, load_stat(d.partials + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
+          st = merge(st, load_stat(a.cta_records + (static_cast<int64_t>(p) * B + b) * IPE_PARTIAL_WORDS));
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) st = merge(st, shfl_xor_stat(st, o));
@@ -928,15 +931,18 @@ size_t tp_parts_bytes(int world, int batch, int hidden) {
   return (2ull * world * batch * (hidden / 2) * kTpLine + 255) / 256 * 256;
 }
 
-size_t decode_step_comm_bytes(int world, int batch, int hidden, int vocab_rows_max) {
-  const size_t parts_max = (static_cast<size_t>(vocab_rows_max) + 31) / 32;
-  return kTpRecv + tp_parts_bytes(world, batch, hidden) + static_cast<size_t>(world) * parts_max * batch * kTpRecordBytes;
+size_t decode_step_comm_bytes(int world, int batch, int hidden) {
+  return kTpRecv + tp_parts_bytes(world, batch, hidden) +
+         static_cast<size_t>(world) * sm_count() * batch * kTpRecordBytes;
 }
 
+// [256 barrier words][attention counters][attention records][the CTAs' merged LM-head records]
 size_t decode_step_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity) {
   (void)capacity;  // attention records are per split, at most kAttnSplitsMax of them
   const size_t counters = (static_cast<size_t>(batch) * kv_heads * sizeof(int) + 255) / 256 * 256;
-  return 256 + counters + static_cast<size_t>(batch) * q_heads * kAttnSplitsMax * kAttnRecord * sizeof(float);
+  const size_t records =
+      (static_cast<size_t>(batch) * q_heads * kAttnSplitsMax * kAttnRecord * sizeof(float) + 255) / 256 * 256;
+  return 256 + counters + records + static_cast<size_t>(sm_count()) * batch * IPE_PARTIAL_WORDS * sizeof(float);
 }
 
 cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStream_t stream, const char** message) {
@@ -949,6 +955,9 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   a.attn_counters = reinterpret_cast<int*>(ws + 256);
   const size_t counters = (static_cast<size_t>(d.batch) * d.kv_heads * sizeof(int) + 255) / 256 * 256;
   a.attn_records = reinterpret_cast<float*>(ws + 256 + counters);
+  const size_t records =
+      (static_cast<size_t>(d.batch) * d.q_heads * kAttnSplitsMax * kAttnRecord * sizeof(float) + 255) / 256 * 256;
+  a.cta_records = reinterpret_cast<float*>(ws + 256 + counters + records);
   const int nt = d.batch <= 8 ? 1 : 2;
   const int group = d.q_heads / d.kv_heads;
   const size_t act = static_cast<size_t>(d.batch) *
@@ -973,8 +982,6 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
       *message = "tensor parallel: needs hidden % 512 == 0 and the activations in shared memory (a smaller batch)";
       return cudaErrorInvalidValue;
     }
-    const int blocks = (d.vocab_total + 31) / 32;
-    a.parts_max = (blocks + d.tp_world - 1) / d.tp_world;
     a.recv_x = kTpRecv;
     a.recv_rec = a.recv_x + tp_parts_bytes(d.tp_world, d.batch, d.hidden);
   }

@@ -98,6 +98,6 @@ size_t comm_slot_offset(int slot, size_t slot_bytes);
 void launch_allreduce_residual(void* x, int64_t count, const uint64_t* peers, int world, int rank, int slot,
                                size_t slot_bytes, int* err, cudaStream_t stream);
 
-size_t decode_step_comm_bytes(int world, int batch, int hidden, int vocab_rows_max);
+size_t decode_step_comm_bytes(int world, int batch, int hidden);
 
 }  // namespace ipe

@@ -234,7 +234,7 @@ class TensorParallelEngine:
         if allreduce == "nvlink":
             self._peer = PeerAllReduce(group, dev, batch * c.hidden_size * 4)
         elif allreduce == "fused":
-            region = int(lib.ipe_decode_step_comm_bytes(self.world, batch, c.hidden_size, 32 * p.parts_max))
+            region = int(lib.ipe_decode_step_comm_bytes(self.world, batch, c.hidden_size))
             self._peer = PeerAllReduce(group, dev, 0, region_bytes=region)
             self.x_alt = torch.empty_like(self.x)
             self.step_ws = torch.zeros(int(lib.ipe_decode_step_workspace(batch, p.q_heads, p.kv_heads, capacity)),
