@@ -366,6 +366,73 @@ def run_tp(args, rank: int, world: int) -> dict | None:
             "clocks": clocks.summary()}
 
 
+def run_load(args) -> dict:
+    """Checkpoint loading onto the GPU (Qwen3-1.7B, random-init, bf16, written once to a temporary
+    directory as two safetensors shards): ipe_b200.weights.load_checkpoint, which streams the
+    payloads through pinned staging buffers into preallocated device tensors, against the
+    reference's procedure restated (one safe_open per file, get_tensor, .to(dtype).to(device) per
+    tensor, the tie check on the device). Wall clock from the call to a synchronized device; the
+    files are in the page cache for both (each is read once untimed first)."""
+    import shutil
+    import tempfile
+
+    from safetensors import safe_open
+
+    from ipe_b200 import QWEN3_1_7B
+    from ipe_b200.checkpoint import LM_HEAD, inspect_checkpoint, write_checkpoint
+    from ipe_b200.synthetic import random_model
+    from ipe_b200.weights import load_checkpoint
+
+    device = torch.device("cuda", 0)
+    model = random_model(QWEN3_1_7B, seed=0, device="cpu", generator_device=device)
+    root = tempfile.mkdtemp(prefix="ipe_ckpt_")
+    try:
+        write_checkpoint(model, root, shard_bytes=2 * 1024**3)
+        del model
+        inventory = inspect_checkpoint(root)
+        total = sum(info.nbytes for info in inventory.values())
+
+        def ours():
+            return load_checkpoint(root, dtype=torch.bfloat16, device=device)
+
+        def restated():
+            loaded = {}
+            for file in sorted({info.file for info in inventory.values()}):
+                with safe_open(f"{root}/{file}", framework="pt", device="cpu") as handle:
+                    for name, info in inventory.items():
+                        if info.file == file:
+                            loaded[name] = handle.get_tensor(name).to(torch.bfloat16).to(device)
+            if LM_HEAD in loaded:
+                torch.equal(loaded["model.embed_tokens.weight"], loaded[LM_HEAD])
+            return loaded
+
+        def timed(fn):
+            torch.cuda.synchronize()
+            start = time.perf_counter()
+            result = fn()
+            torch.cuda.synchronize()
+            elapsed = time.perf_counter() - start
+            del result
+            torch.cuda.empty_cache()
+            return elapsed
+
+        timed(restated)  # page cache warm for both
+        ours_s = [timed(ours) for _ in range(max(1, args.steps))]
+        ref_s = [timed(restated) for _ in range(max(1, args.steps))]
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
+    best, ref_best = min(ours_s), min(ref_s)
+    return {"metric": "checkpoint load GB/s, Qwen3-1.7B bf16 safetensors -> GPU", "value": round(total / best / 1e9, 3),
+            "unit": "GB/s", "n_gpus": 1, "steps": len(ours_s), "warmup": 1, "higher_is_better": True,
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init), 2 safetensors shards, page cache warm",
+            "config": {"workload": f"load {total} bytes of Qwen3-1.7B weights to cuda:0"},
+            "seconds": [round(t, 4) for t in ours_s],
+            "reference_procedure": {"value": round(total / ref_best / 1e9, 3), "unit": "GB/s",
+                                    "seconds": [round(t, 4) for t in ref_s],
+                                    "what": "safe_open + get_tensor + .to(bf16).to(cuda) per tensor "
+                                            "(src/ipe/weights.py:154-161)"}}
+
+
 def cpu_baseline(workload: str, samples: int) -> dict:
     """The reference engine's algorithm (oracle/ restatement, bf16, sdpa) on the host cores:
     one prefill of the workload's prompt, then `samples` decode steps (bounded sample)."""
@@ -446,10 +513,13 @@ def main() -> None:
     parser.add_argument("--layers", type=int, default=0, help="fewer decoder layers (profiling only; not a bench line)")
     parser.add_argument("--tp", action="store_true", help="tensor-parallel B=1 latency mode over the launched ranks")
     parser.add_argument("--tp-allreduce", default="fused", choices=("fused", "nvlink", "nccl"))
+    parser.add_argument("--load", action="store_true", help="checkpoint loading to the GPU instead of generation")
     args = parser.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
         line = run_reference(args, rank)
+    elif args.load:
+        line = run_load(args) if rank == 0 else None
     else:
         if world > 1:
             import datetime

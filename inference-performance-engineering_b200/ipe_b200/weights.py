@@ -3,10 +3,12 @@
 Field names, order and layout ([out, in]) follow the reference's dataclasses
 (`src/ipe/weights.py:38-75`): a `LoadedCheckpoint` built by the reference's loader can be passed
 to this package unchanged, and the reverse. `lm_head is embed_tokens` whenever the head is tied.
-Loading safetensors files is not part of this package; see `ipe_b200.synthetic` for the
-random-init models the benchmarks use.
+`load_checkpoint` reads a Transformers-style safetensors checkpoint directory, streaming the
+payloads straight to the GPU; `ipe_b200.synthetic` builds the random-init models the benchmarks
+use.
 """
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -54,3 +56,144 @@ class LoadedCheckpoint:
     config: Qwen3Config
     weights: Qwen3Weights
     tie: TieRecord
+
+
+# ------------------------------------------------------------------------------------ loading
+
+# Rows per chunk when comparing the embedding with a stored head (bounds the fp32 temporaries).
+_DIFF_ROWS = 4096
+STAGING_BYTES = 64 * 1024 * 1024
+
+
+def _check_arguments(dtype: torch.dtype, device) -> torch.device:
+    if dtype not in DTYPES:
+        raise ValueError(f"dtype {dtype!r}: expected one of {list(DTYPES)}")
+    if not isinstance(device, (str, torch.device)):
+        raise ValueError(f"device {device!r}: expected a string or torch.device")
+    try:
+        device = torch.device(device)
+    except RuntimeError as error:
+        raise ValueError(f"device {device!r}: {error}") from error
+    if device.type == "cpu":
+        if device.index not in (None, 0):
+            raise ValueError(f"device {device}: only index 0 exists")
+    elif device.type == "cuda":
+        if not torch.cuda.is_available():
+            raise ValueError("device cuda: not available")
+        if device.index is not None and device.index >= torch.cuda.device_count():
+            raise ValueError(f"device {device}: only {torch.cuda.device_count()} CUDA device(s)")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+    else:
+        raise ValueError(f"device {device}: expected cpu or cuda")
+    return device
+
+
+def _max_abs_diff(a: torch.Tensor, b: torch.Tensor) -> float:
+    """fp32 max |a - b| over unequal positions (equal ones count 0, so equal infinities give 0)."""
+    result = torch.zeros((), dtype=torch.float32, device=a.device)
+    for start in range(0, a.shape[0], _DIFF_ROWS):
+        x, y = a[start:start + _DIFF_ROWS].float(), b[start:start + _DIFF_ROWS].float()
+        result = torch.maximum(result, torch.where(x == y, 0.0, (x - y).abs()).amax())
+    return result.item()
+
+
+def _tie_record(stored: dict[str, torch.Tensor]) -> TieRecord:
+    """Tied when the head is not stored, or equals the embedding in value (torch.equal: +0 equals
+    -0, NaN equals nothing), as src/ipe/weights.py:113-124 decides it."""
+    from ipe_b200.checkpoint import EMBED_TOKENS, LM_HEAD
+
+    if LM_HEAD not in stored:
+        return TieRecord(stored=False, tied=True, max_abs_diff=None)
+    embed, head = stored[EMBED_TOKENS], stored[LM_HEAD]
+    tied = torch.equal(embed, head)
+    return TieRecord(stored=True, tied=tied, max_abs_diff=0.0 if tied else _max_abs_diff(embed, head))
+
+
+def _read_cpu(root, inventory) -> dict[str, torch.Tensor]:
+    """bf16 CPU tensors as copy-on-write views of one private mapping per file."""
+    import mmap
+
+    stored = {}
+    for file in sorted({info.file for info in inventory.values()}):
+        with open(root / file, "rb") as handle:
+            mapping = mmap.mmap(handle.fileno(), 0, access=mmap.ACCESS_COPY) if (root / file).stat().st_size else None
+        for name, info in inventory.items():
+            if info.file != file:
+                continue
+            if info.nbytes == 0:
+                stored[name] = torch.empty(info.shape, dtype=torch.bfloat16)
+            else:
+                flat = torch.frombuffer(mapping, dtype=torch.bfloat16, count=info.nbytes // 2, offset=info.offset)
+                stored[name] = flat.view(info.shape)
+    return stored
+
+
+def _read_cuda(root, inventory, device: torch.device, staging_bytes: int) -> dict[str, torch.Tensor]:
+    """bf16 device tensors, each file's payloads streamed in file order by ipe_read_to_device."""
+    from ipe_b200 import _native as nat
+
+    lib = nat.load()
+    stored = {name: torch.empty(info.shape, dtype=torch.bfloat16, device=device) for name, info in inventory.items()}
+    stream = torch.cuda.current_stream(device).cuda_stream
+    for file in sorted({info.file for info in inventory.values()}):
+        names = sorted((n for n, i in inventory.items() if i.file == file and i.nbytes), key=lambda n: inventory[n].offset)
+        count = len(names)
+        offsets = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].offset for n in names])
+        sizes = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].nbytes for n in names])
+        dsts = (ctypes.c_void_p * max(count, 1))(*[stored[n].data_ptr() for n in names])
+        status = lib.ipe_read_to_device(str(root / file).encode(), count, offsets, sizes, dsts, staging_bytes, stream)
+        if status == 4:  # IPE_ERR_IO
+            raise OSError(lib.ipe_last_error().decode(errors="replace"))
+        nat.check(status, "ipe_read_to_device")
+    return stored
+
+
+def load_checkpoint(directory, *, dtype: torch.dtype, device, staging_bytes: int = STAGING_BYTES) -> LoadedCheckpoint:
+    """Validate a checkpoint directory from its headers, then load its tensors at `dtype` on
+    `device` (src/ipe/weights.py:135-168).
+
+    dtype is bfloat16, float32 or float64; device is cpu or an available CUDA device. On a CUDA
+    device every payload is streamed from the files straight into its device tensor through two
+    pinned staging buffers (the file read of one chunk overlapping the copy of the last); wider
+    dtypes are exact casts made on the device. On the CPU, bf16 tensors are copy-on-write views of
+    the files. A stored LM head equal to the embedding is dropped and lm_head is the embedding
+    itself. If loading fails after the checks, every held tensor is dropped and the callee frames
+    are cleared, so a traceback kept by the caller does not pin the weights. Errors: ValueError
+    for dtype or device, ConfigError, CheckpointError, OSError for file access.
+    """
+    import traceback
+    from pathlib import Path
+
+    from ipe_b200.checkpoint import EMBED_TOKENS, FINAL_NORM, LAYER_TENSORS, LM_HEAD, check_mapping, \
+        inspect_checkpoint, read_config
+
+    device = _check_arguments(dtype, device)
+    root = Path(directory)
+    config = read_config(root / "config.json")
+    inventory = inspect_checkpoint(root)
+    check_mapping(inventory, config)
+    stored: dict[str, torch.Tensor] = {}
+    loaded: dict[str, torch.Tensor] = {}
+    try:
+        if device.type == "cuda":
+            with torch.cuda.device(device):
+                stored = _read_cuda(root, inventory, device, int(staging_bytes))
+        else:
+            stored = _read_cpu(root, inventory)
+        tie = _tie_record(stored)
+        for name in inventory:
+            if not (tie.tied and name == LM_HEAD):
+                loaded[name] = stored[name] if dtype == torch.bfloat16 else stored[name].to(dtype)
+        stored.clear()
+        embed = loaded[EMBED_TOKENS]
+        layers = tuple(
+            LayerWeights(**{field: loaded[f"model.layers.{layer}.{suffix}"] for field, suffix in LAYER_TENSORS.items()})
+            for layer in range(config.num_hidden_layers))
+        weights = Qwen3Weights(embed, layers, loaded[FINAL_NORM], embed if tie.tied else loaded[LM_HEAD])
+    except BaseException as error:
+        stored.clear()
+        loaded.clear()
+        traceback.clear_frames(error.__traceback__.tb_next)
+        raise
+    return LoadedCheckpoint(config, weights, tie)
