@@ -433,6 +433,106 @@ def run_load(args) -> dict:
                                             "(src/ipe/weights.py:154-161)"}}
 
 
+def run_compare(args) -> dict:
+    """The reference harness's engine comparison (bench/run.py:96-144): the workload's greedy
+    generation through each engine's own public API from one checkpoint directory (the random-init
+    Qwen3-1.7B written once), host wall clock from the call to a synchronized device, and the
+    harness's TPOT = (latency(N) - latency(1)) / (N - 1), prefill = latency(1). Engines: this one
+    (load_checkpoint + Engine.generate), Transformers with a static cache (Qwen3ForCausalLM,
+    sdpa, bf16), and vLLM (tokens in, no tokenizer, ignore_eos), each where it imports."""
+    import gc
+    import shutil
+    import tempfile
+
+    from ipe_b200 import QWEN3_1_7B
+    from ipe_b200.checkpoint import write_checkpoint
+    from ipe_b200.engine import Engine
+    from ipe_b200.synthetic import random_model
+    from ipe_b200.weights import load_checkpoint
+
+    batch, prompt, new, capacity, _ = WORKLOADS[args.workload]
+    device = torch.device("cuda", 0)
+    root = tempfile.mkdtemp(prefix="ipe_compare_")
+    ids = torch.randint(0, QWEN3_1_7B.vocab_size, (batch, prompt), generator=torch.Generator().manual_seed(0))
+    engines = {}
+    try:
+        write_checkpoint(random_model(QWEN3_1_7B, seed=0, device="cpu", generator_device=device), root,
+                         shard_bytes=2 * 1024**3)
+
+        def measure(generate) -> dict:
+            def latency(n):
+                torch.cuda.synchronize()
+                start = time.perf_counter()
+                tokens = generate(n)
+                torch.cuda.synchronize()
+                elapsed = time.perf_counter() - start
+                if tuple(tokens.shape) != (batch, n):
+                    raise RuntimeError(f"expected {n} new tokens per row, got {tuple(tokens.shape)}")
+                return elapsed, tokens
+
+            for _ in range(max(1, args.warmup)):
+                latency(new)
+            full, first, tokens = [], [], None
+            for _ in range(max(1, args.steps)):
+                t, tokens = latency(new)
+                full.append(t)
+                first.append(latency(1)[0])
+            tpot = (statistics.median(full) - statistics.median(first)) / (new - 1)
+            return {"decode_tok_s": round(batch / tpot, 2), "tpot_ms": round(tpot * 1e3, 4),
+                    "prefill_ms": round(statistics.median(first) * 1e3, 3),
+                    "latency_s": [round(t, 4) for t in full], "first_tokens": tokens[0, :8].tolist()}
+
+        engine = Engine(load_checkpoint(root, dtype=torch.bfloat16, device=device), batch=batch, capacity=capacity)
+        engines["ipe_b200"] = measure(lambda n: engine.generate(ids, n).tokens)
+        del engine
+        gc.collect()
+        torch.cuda.empty_cache()
+        try:
+            from transformers import GenerationConfig, Qwen3ForCausalLM
+
+            model = Qwen3ForCausalLM.from_pretrained(root, dtype=torch.bfloat16, attn_implementation="sdpa")
+            model = model.to(device).eval()
+            model.generation_config.eos_token_id = None
+            config = GenerationConfig(do_sample=False, eos_token_id=None, pad_token_id=0, cache_implementation="static")
+            prompt_d, mask = ids.to(device), torch.ones_like(ids, device=device)
+
+            def hf(n):
+                with torch.no_grad():
+                    out = model.generate(prompt_d, attention_mask=mask, generation_config=config, max_new_tokens=n)
+                return out[:, prompt:].cpu()
+
+            engines["transformers_static"] = measure(hf)
+            del model
+        except Exception as error:  # noqa: BLE001 - an engine that does not run is reported, not fatal
+            engines["transformers_static"] = {"unavailable": f"{type(error).__name__}: {error}"[:300]}
+        gc.collect()
+        torch.cuda.empty_cache()
+        try:
+            from vllm import LLM, SamplingParams, TokensPrompt
+
+            llm = LLM(model=root, dtype="bfloat16", enable_prefix_caching=False, seed=0, max_model_len=capacity,
+                      max_num_seqs=batch, skip_tokenizer_init=True, gpu_memory_utilization=0.5)
+            prompts = [TokensPrompt(prompt_token_ids=row.tolist()) for row in ids]
+
+            def vllm_generate(n):
+                params = SamplingParams(max_tokens=n, temperature=0.0, ignore_eos=True, detokenize=False)
+                outputs = llm.generate(prompts, params, use_tqdm=False)
+                return torch.tensor([list(o.outputs[0].token_ids) for o in outputs])
+
+            engines["vllm"] = measure(vllm_generate)
+            del llm
+        except Exception as error:  # noqa: BLE001
+            engines["vllm"] = {"unavailable": f"{type(error).__name__}: {error}"[:300]}
+    finally:
+        shutil.rmtree(root, ignore_errors=True)
+    ours = engines["ipe_b200"]["decode_tok_s"]
+    return {"metric": f"decode tok/s by TPOT (harness wall clock), Qwen3-1.7B bf16, {args.workload}", "value": ours,
+            "unit": "decode tok/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init checkpoint written once)",
+            "config": {"workload": f"{args.workload}: batch {batch}, prompt {prompt}, {new} new tokens, greedy"},
+            "engines": engines}
+
+
 def cpu_baseline(workload: str, samples: int) -> dict:
     """The reference engine's algorithm (oracle/ restatement, bf16, sdpa) on the host cores:
     one prefill of the workload's prompt, then `samples` decode steps (bounded sample)."""
@@ -514,12 +614,16 @@ def main() -> None:
     parser.add_argument("--tp", action="store_true", help="tensor-parallel B=1 latency mode over the launched ranks")
     parser.add_argument("--tp-allreduce", default="fused", choices=("fused", "nvlink", "nccl"))
     parser.add_argument("--load", action="store_true", help="checkpoint loading to the GPU instead of generation")
+    parser.add_argument("--compare", action="store_true",
+                        help="this engine against Transformers (static cache) and vLLM on the workload")
     args = parser.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
         line = run_reference(args, rank)
     elif args.load:
         line = run_load(args) if rank == 0 else None
+    elif args.compare:
+        line = run_compare(args) if rank == 0 else None
     else:
         if world > 1:
             import datetime

@@ -62,7 +62,8 @@ class LoadedCheckpoint:
 
 # Rows per chunk when comparing the embedding with a stored head (bounds the fp32 temporaries).
 _DIFF_ROWS = 4096
-STAGING_BYTES = 64 * 1024 * 1024
+STAGING_BYTES = 16 * 1024 * 1024  # per staging buffer; each reader thread has two
+READERS = 8
 
 
 def _check_arguments(dtype: torch.dtype, device) -> torch.device:
@@ -129,7 +130,7 @@ def _read_cpu(root, inventory) -> dict[str, torch.Tensor]:
     return stored
 
 
-def _read_cuda(root, inventory, device: torch.device, staging_bytes: int) -> dict[str, torch.Tensor]:
+def _read_cuda(root, inventory, device: torch.device, staging_bytes: int, readers: int) -> dict[str, torch.Tensor]:
     """bf16 device tensors, each file's payloads streamed in file order by ipe_read_to_device."""
     from ipe_b200 import _native as nat
 
@@ -142,21 +143,23 @@ def _read_cuda(root, inventory, device: torch.device, staging_bytes: int) -> dic
         offsets = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].offset for n in names])
         sizes = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].nbytes for n in names])
         dsts = (ctypes.c_void_p * max(count, 1))(*[stored[n].data_ptr() for n in names])
-        status = lib.ipe_read_to_device(str(root / file).encode(), count, offsets, sizes, dsts, staging_bytes, stream)
+        status = lib.ipe_read_to_device(str(root / file).encode(), count, offsets, sizes, dsts, staging_bytes, readers,
+                                        stream)
         if status == 4:  # IPE_ERR_IO
             raise OSError(lib.ipe_last_error().decode(errors="replace"))
         nat.check(status, "ipe_read_to_device")
     return stored
 
 
-def load_checkpoint(directory, *, dtype: torch.dtype, device, staging_bytes: int = STAGING_BYTES) -> LoadedCheckpoint:
+def load_checkpoint(directory, *, dtype: torch.dtype, device, staging_bytes: int = STAGING_BYTES,
+                    readers: int = READERS) -> LoadedCheckpoint:
     """Validate a checkpoint directory from its headers, then load its tensors at `dtype` on
     `device` (src/ipe/weights.py:135-168).
 
     dtype is bfloat16, float32 or float64; device is cpu or an available CUDA device. On a CUDA
-    device every payload is streamed from the files straight into its device tensor through two
-    pinned staging buffers (the file read of one chunk overlapping the copy of the last); wider
-    dtypes are exact casts made on the device. On the CPU, bf16 tensors are copy-on-write views of
+    device every payload is streamed from the files straight into its device tensor by `readers`
+    threads, each reading chunks of up to staging_bytes into one of its two pinned buffers while
+    the other's host-to-device copy runs; wider dtypes are exact casts made on the device. On the CPU, bf16 tensors are copy-on-write views of
     the files. A stored LM head equal to the embedding is dropped and lm_head is the embedding
     itself. If loading fails after the checks, every held tensor is dropped and the callee frames
     are cleared, so a traceback kept by the caller does not pin the weights. Errors: ValueError
@@ -178,7 +181,7 @@ def load_checkpoint(directory, *, dtype: torch.dtype, device, staging_bytes: int
     try:
         if device.type == "cuda":
             with torch.cuda.device(device):
-                stored = _read_cuda(root, inventory, device, int(staging_bytes))
+                stored = _read_cuda(root, inventory, device, int(staging_bytes), int(readers))
         else:
             stored = _read_cpu(root, inventory)
         tie = _tie_record(stored)

@@ -36,10 +36,10 @@ def _assert_same(gpu, cpu):
             assert torch.equal(getattr(lg, field).cpu(), getattr(lc, field)), field
 
 
-@pytest.mark.parametrize("shard_bytes", [None, 700_000])
-def test_cuda_load_equals_the_source(small, tmp_path, shard_bytes):
+@pytest.mark.parametrize("shard_bytes, readers", [(None, 1), (None, 8), (700_000, 3)])
+def test_cuda_load_equals_the_source(small, tmp_path, shard_bytes, readers):
     write_checkpoint(small, tmp_path, shard_bytes=shard_bytes)
-    gpu = load_checkpoint(tmp_path, dtype=torch.bfloat16, device="cuda", staging_bytes=64 * 1024)
+    gpu = load_checkpoint(tmp_path, dtype=torch.bfloat16, device="cuda", staging_bytes=64 * 1024, readers=readers)
     _assert_same(gpu, small)
     assert gpu.weights.lm_head is gpu.weights.embed_tokens
     assert (gpu.tie.stored, gpu.tie.tied) == (False, True)
