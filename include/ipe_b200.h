@@ -365,16 +365,18 @@ int ipe_decode_step_grid(void);
  * src/ipe/engine.py:84-111 (decode -> _step) and, with sampling, one iteration of
  * src/ipe/engine.py:137-147. */
 int ipe_decode_step(const ipe_decode_step_desc* desc, void* stream);
-/* Checkpoint loading. Reads `count` byte ranges [offsets[i], offsets[i] + sizes[i]) of the file at
- * `path` into device memory at destinations[i] (current device), in chunks of at most
- * staging_bytes taken in file order by `threads` (1..64) reader threads, each with two pinned
- * staging buffers of staging_bytes: a reader fills one buffer while the host-to-device copy of the
- * other (on `stream`) runs. Returns once every copy has finished. IPE_ERR_IO when the file cannot be opened
- * or read (ipe_last_error names it), IPE_ERR_ARGUMENT for a range outside the file. Replaces the
- * per-tensor mmap -> .to(dtype) -> .to(device) copies of src/ipe/weights.py:154-161 (the
- * safetensors payload offsets come from the file headers, parsed by the caller). */
-int ipe_read_to_device(const char* path, int count, const uint64_t* offsets, const uint64_t* sizes,
-                       void* const* destinations, size_t staging_bytes, int threads, void* stream);
+/* Checkpoint loading. Reads `count` byte ranges [offsets[i], offsets[i] + sizes[i]) of file
+ * paths[file_of[i]] (of `files` files) into device memory at destinations[i] (current device), in
+ * chunks of at most staging_bytes taken in list order by `threads` (1..64) reader threads, each
+ * with two pinned staging buffers of staging_bytes: a reader fills one buffer while the
+ * host-to-device copy of the other (on `stream`) runs. Returns once every copy has finished.
+ * IPE_ERR_IO when a file cannot be opened or read (ipe_last_error names it), IPE_ERR_ARGUMENT for
+ * a range outside its file. Replaces the per-tensor mmap -> .to(dtype) -> .to(device) copies of
+ * src/ipe/weights.py:154-161 (the safetensors payload offsets come from the file headers, parsed
+ * by the caller). */
+int ipe_read_to_device(int files, const char* const* paths, int count, const int* file_of, const uint64_t* offsets,
+                       const uint64_t* sizes, void* const* destinations, size_t staging_bytes, int threads,
+                       void* stream);
 
 /* Bytes of one rank's communication region for a tensor-parallel decode step on this device: the
  * epoch counter, two receive slots of every rank's row-parallel part, and every rank's per-CTA

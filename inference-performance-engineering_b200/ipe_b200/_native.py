@@ -51,7 +51,7 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "ipe_decode_step_workspace": (c_size_t, [c_int, c_int, c_int, c_int]),
     "ipe_decode_step_grid": (c_int, []),
     "ipe_decode_step_comm_bytes": (c_size_t, [c_int, c_int, c_int]),
-    "ipe_read_to_device": (c_int, [ctypes.c_char_p, c_int, _P, _P, _P, c_size_t, c_int, _P]),
+    "ipe_read_to_device": (c_int, [c_int, _P, c_int, _P, _P, _P, _P, c_size_t, c_int, _P]),
     "ipe_gemm_f32": (c_int, [_P, _P, _P, c_int, c_int, c_int, c_int, _P, _P]),
     "ipe_embed_f32": (c_int, [_P, c_int64, _P, c_int64, c_int, _P, _P]),
     "ipe_qk_norm_rope_append_f32": (c_int, [_P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, c_int, _P, _P, _P, c_int,

@@ -62,7 +62,7 @@ class LoadedCheckpoint:
 
 # Rows per chunk when comparing the embedding with a stored head (bounds the fp32 temporaries).
 _DIFF_ROWS = 4096
-STAGING_BYTES = 16 * 1024 * 1024  # per staging buffer; each reader thread has two
+STAGING_BYTES = 4 * 1024 * 1024  # per staging buffer; each reader thread has two
 READERS = 8
 
 
@@ -131,23 +131,42 @@ def _read_cpu(root, inventory) -> dict[str, torch.Tensor]:
 
 
 def _read_cuda(root, inventory, device: torch.device, staging_bytes: int, readers: int) -> dict[str, torch.Tensor]:
-    """bf16 device tensors, each file's payloads streamed in file order by ipe_read_to_device."""
+    """bf16 device tensors, carved (256-byte aligned) from one device allocation, since hundreds of
+    separate allocations cost far more than the reads; a stored LM head gets its own allocation,
+    so that dropping it when tied frees it. Every payload of every file is streamed by one
+    ipe_read_to_device call."""
     from ipe_b200 import _native as nat
+    from ipe_b200.checkpoint import LM_HEAD
 
     lib = nat.load()
-    stored = {name: torch.empty(info.shape, dtype=torch.bfloat16, device=device) for name, info in inventory.items()}
+    align = 256
+    names = [n for n in inventory if n != LM_HEAD]
+    layout, total = {}, 0
+    for name in names:
+        layout[name] = total
+        total += (inventory[name].nbytes + align - 1) // align * align
+    block = torch.empty(max(total, align), dtype=torch.uint8, device=device)
+    stored = {}
+    for name in names:
+        info = inventory[name]
+        stored[name] = block[layout[name]:layout[name] + info.nbytes].view(torch.bfloat16).view(info.shape)
+    if LM_HEAD in inventory:
+        stored[LM_HEAD] = torch.empty(inventory[LM_HEAD].shape, dtype=torch.bfloat16, device=device)
+    files = sorted({info.file for info in inventory.values()})
+    ranges = sorted((n for n, i in inventory.items() if i.nbytes), key=lambda n: (files.index(inventory[n].file),
+                                                                                 inventory[n].offset))
+    count = len(ranges)
+    paths = (ctypes.c_char_p * len(files))(*[str(root / f).encode() for f in files])
+    file_of = (ctypes.c_int * max(count, 1))(*[files.index(inventory[n].file) for n in ranges])
+    offsets = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].offset for n in ranges])
+    sizes = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].nbytes for n in ranges])
+    dsts = (ctypes.c_void_p * max(count, 1))(*[stored[n].data_ptr() for n in ranges])
     stream = torch.cuda.current_stream(device).cuda_stream
-    for file in sorted({info.file for info in inventory.values()}):
-        names = sorted((n for n, i in inventory.items() if i.file == file and i.nbytes), key=lambda n: inventory[n].offset)
-        count = len(names)
-        offsets = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].offset for n in names])
-        sizes = (ctypes.c_uint64 * max(count, 1))(*[inventory[n].nbytes for n in names])
-        dsts = (ctypes.c_void_p * max(count, 1))(*[stored[n].data_ptr() for n in names])
-        status = lib.ipe_read_to_device(str(root / file).encode(), count, offsets, sizes, dsts, staging_bytes, readers,
-                                        stream)
-        if status == 4:  # IPE_ERR_IO
-            raise OSError(lib.ipe_last_error().decode(errors="replace"))
-        nat.check(status, "ipe_read_to_device")
+    status = lib.ipe_read_to_device(len(files), paths, count, file_of, offsets, sizes, dsts, staging_bytes, readers,
+                                    stream)
+    if status == 4:  # IPE_ERR_IO
+        raise OSError(lib.ipe_last_error().decode(errors="replace"))
+    nat.check(status, "ipe_read_to_device")
     return stored
 
 

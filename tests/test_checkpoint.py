@@ -212,14 +212,17 @@ def test_native_reader_rejects_bad_ranges_and_missing_files(tiny, tmp_path):
 
     write_checkpoint(tiny, tmp_path)
     lib = nat.load()
-    path = str(tmp_path / SINGLE_FILE).encode()
+    paths = (ctypes.c_char_p * 1)(str(tmp_path / SINGLE_FILE).encode())
+    missing = (ctypes.c_char_p * 1)(str(tmp_path / "none").encode())
     size = (tmp_path / SINGLE_FILE).stat().st_size
-    offsets, sizes = (ctypes.c_uint64 * 1)(size - 4), (ctypes.c_uint64 * 1)(8)
+    file_of, offsets, sizes = (ctypes.c_int * 1)(0), (ctypes.c_uint64 * 1)(size - 4), (ctypes.c_uint64 * 1)(8)
     dsts = (ctypes.c_void_p * 1)(16)
-    assert lib.ipe_read_to_device(path, 1, offsets, sizes, dsts, 1 << 20, 2, None) == 1
+    assert lib.ipe_read_to_device(1, paths, 1, file_of, offsets, sizes, dsts, 1 << 20, 2, None) == 1
     assert b"outside" in lib.ipe_last_error()
-    assert lib.ipe_read_to_device(str(tmp_path / "none").encode(), 1, offsets, sizes, dsts, 1 << 20, 2, None) == 4
+    assert lib.ipe_read_to_device(1, missing, 1, file_of, offsets, sizes, dsts, 1 << 20, 2, None) == 4
     assert b"cannot open" in lib.ipe_last_error()
-    assert lib.ipe_read_to_device(path, 0, None, None, None, 1 << 20, 2, None) == 0
-    assert lib.ipe_read_to_device(path, 1, offsets, sizes, dsts, 100, 2, None) == 1
-    assert lib.ipe_read_to_device(path, 1, offsets, sizes, dsts, 1 << 20, 0, None) == 1
+    assert lib.ipe_read_to_device(1, paths, 0, None, None, None, None, 1 << 20, 2, None) == 0
+    assert lib.ipe_read_to_device(1, paths, 1, file_of, offsets, sizes, dsts, 100, 2, None) == 1
+    bad_file = (ctypes.c_int * 1)(1)
+    assert lib.ipe_read_to_device(1, paths, 1, bad_file, offsets, sizes, dsts, 1 << 20, 2, None) == 1
+    assert lib.ipe_read_to_device(1, paths, 1, file_of, offsets, sizes, dsts, 1 << 20, 0, None) == 1
