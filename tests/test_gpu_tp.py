@@ -1,8 +1,8 @@
-"""The tensor-parallel engine on 2 GPUs in its three step modes (the one-kernel step with its
+"""The tensor-parallel engine on 2 (and, where the box has them, 4 and 8) GPUs in its three step modes (the one-kernel step with its
 exchanges inside, per-operator kernels with the peer-memory all-reduce, and with NCCL) against the
 single-GPU engine: teacher-forced logits within a few bf16 ulps (the same math; fp32 partial sums
-added in another order) and the same greedy tokens on every rank. Needs two GPUs; skipped
-otherwise."""
+added in another order) and the same greedy tokens on every rank. Each world size is skipped on a
+box with fewer GPUs."""
 
 import datetime
 import os
@@ -16,7 +16,6 @@ import torch.multiprocessing as mp
 from cases import build, to_device
 
 pytestmark = pytest.mark.gpu
-WORLD = 2
 MODES = ("fused", "nvlink", "nccl")
 
 
@@ -61,12 +60,15 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs two GPUs")
-def test_tensor_parallel_engine_matches_the_single_gpu_engine(tmp_path):
-    mp.spawn(_worker, args=(WORLD, _free_port(), str(tmp_path)), nprocs=WORLD, join=True)
-    r0, r1 = torch.load(tmp_path / "rank0.pt"), torch.load(tmp_path / "rank1.pt")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_engine_matches_the_single_gpu_engine(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    ranks = [torch.load(tmp_path / f"rank{r}.pt") for r in range(world)]
+    r0 = ranks[0]
     ref = r0["logits"]
-    for r in (r0, r1):
+    for r in ranks:
         assert r["device_error"] == 0
         for mode in MODES:
             assert ((r[f"tp_logits_{mode}"] - ref).abs() <= 4 * 2 ** -8 * ref.abs() + 0.05).all()
