@@ -73,8 +73,8 @@ def test_tensor_parallel_engine_matches_the_single_gpu_engine(tmp_path, world):
         for mode in MODES:
             assert ((r[f"tp_logits_{mode}"] - ref).abs() <= 4 * 2 ** -8 * ref.abs() + 0.05).all()
             assert torch.equal(r[f"tokens_{mode}"], r0[f"tokens_{mode}"])  # every rank samples the same tokens
-        # two addends sum to the same bits in either order: the peer-memory all-reduce equals NCCL's
-        assert torch.equal(r["tp_logits_nvlink"], r["tp_logits_nccl"])
+        if world == 2:  # two addends sum to the same bits in either order: the peer-memory all-reduce
+            assert torch.equal(r["tp_logits_nvlink"], r["tp_logits_nccl"])  # equals NCCL's (not so for more)
     for mode in MODES:
         agree = (r0[f"tokens_{mode}"] == r0["ref_tokens"]).float().mean()
         assert agree > 0.9, (mode, r0[f"tokens_{mode}"], r0["ref_tokens"])
