@@ -1,0 +1,136 @@
+"""Per-phase timeline of the one-kernel decode step, from its device trace (`ipe_decode_step_desc.trace`).
+
+    python -m ipe_b200.steptrace [--batch B] [--prompt P]                # one GPU, Engine
+    torchrun --nproc-per-node N -m ipe_b200.steptrace --tp [...]         # N ranks, fused TP step
+
+Builds the random-init Qwen3-1.7B (seed 0, drawn on the GPU), prefills a random prompt, runs a
+few generation steps, then times 20 untraced steps (CUDA events) and one traced step, and prints
+for each phase kind (embedding, QKV, attention, o_proj, gate/up, down_proj, LM head), summed over
+the step's layers:
+- stage: from the end of the previous phase (a grid-barrier release, or in a tensor-parallel step
+  this CTA's own end of a row-parallel phase) to the phase's activations staged, worst CTA; in a
+  tensor-parallel step it includes waiting for the peers' parts;
+- work: from the earliest CTA staged to the last CTA's end of the phase;
+- barrier: from the last arrival to the first release (negative when the phase ends without a
+  grid barrier, as the row-parallel phases of a tensor-parallel step do);
+and the sampling tail (CTA 0's exit after the last CTA's end of the LM head).
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import os
+
+import torch
+
+from ipe_b200 import _native as nat
+
+KINDS = ("qkv", "attn", "o", "gu", "down")
+
+
+def traced_step(desc, grid: int, layers: int, stream: int, device: torch.device) -> torch.Tensor:
+    """Run one decode step described by `desc` (an ipe_decode_step_desc) with tracing on; returns
+    the raw trace [grid, IPE_TRACE_WORDS(layers)] of globaltimer nanoseconds."""
+    trace = torch.zeros(grid, nat.trace_words(layers), dtype=torch.int64, device=device)
+    traced = nat.StepDesc.from_buffer_copy(desc)
+    traced.trace = trace.data_ptr()
+    nat.check(nat.load().ipe_decode_step(ctypes.addressof(traced), stream), "ipe_decode_step")
+    torch.cuda.synchronize(device)
+    return trace.cpu()
+
+
+def summarize(raw: torch.Tensor, layers: int) -> dict:
+    """Per phase kind: [stage, work, barrier] microseconds summed over the step, and the totals."""
+    words = nat.trace_words(layers)
+    t = (raw - raw[:, 0].min()).double() / 1000.0
+    ends = 5 * layers + 2
+    table: dict[str, list[float]] = {}
+    for p in range(1, ends + 1):
+        b = 1 + 5 * (p - 1)
+        kind = "embed" if p == 1 else ("lm" if p == ends else KINDS[(p - 2) % 5])
+        start = t[:, b - 4] if p > 1 else t[:, 0]
+        staged = t[:, b - 3] if p > 1 else t[:, 0]
+        row = table.setdefault(kind, [0.0, 0.0, 0.0])
+        row[0] += (staged - start).max().item()
+        if kind != "attn":  # attention marks no staging; its work is in the barrier that follows
+            row[1] += (t[:, b].max() - staged.min()).item()
+        row[2] += (t[:, b + 1].min() - t[:, b].max()).item()
+    lm_end = t[:, words - 2].max().item()
+    return {"phases": table, "lm_end_us": lm_end, "sampling_tail_us": t[0, words - 1].item() - lm_end}
+
+
+def format_summary(summary: dict, untraced_us: float, label: str) -> str:
+    lines = [f"{label}: untraced step {untraced_us:.1f} us; LM head done at {summary['lm_end_us']:.1f} us; "
+             f"sampling tail {summary['sampling_tail_us']:.1f} us",
+             f"{'phase':6s} {'stage':>8s} {'work':>8s} {'barrier':>8s}   (us, summed over the step)"]
+    for kind, (stage, work, barrier) in summary["phases"].items():
+        lines.append(f"{kind:6s} {stage:8.1f} {work:8.1f} {barrier:8.1f}")
+    return "\n".join(lines)
+
+
+def main() -> None:
+    import datetime
+
+    from ipe_b200 import QWEN3_1_7B
+    from ipe_b200.synthetic import random_model
+
+    parser = argparse.ArgumentParser(prog="python -m ipe_b200.steptrace")
+    parser.add_argument("--batch", type=int, default=1)
+    parser.add_argument("--prompt", type=int, default=512)
+    parser.add_argument("--tp", action="store_true", help="tensor-parallel fused step over the torchrun ranks")
+    args = parser.parse_args()
+    rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+    device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(device)
+    if args.tp:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    loaded = random_model(QWEN3_1_7B, seed=0, device=device, generator_device=device)
+    ids = torch.randint(0, QWEN3_1_7B.vocab_size, (args.batch, args.prompt), generator=torch.Generator().manual_seed(0))
+    if args.tp:
+        from ipe_b200.tp import TensorParallelEngine
+
+        engine = TensorParallelEngine(loaded, batch=args.batch, capacity=args.prompt + 64, allreduce="fused")
+        engine.generate(ids, 8)
+        desc = engine._step_desc(True)
+    else:
+        from ipe_b200.engine import Engine
+
+        engine = Engine(loaded, batch=args.batch, capacity=args.prompt + 64)
+        engine.generate(ids, 8)
+        desc = engine._step_descs[(args.batch, True)]
+    lib = nat.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    layers = QWEN3_1_7B.num_hidden_layers
+    if args.tp:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(20):
+        nat.check(lib.ipe_decode_step(ctypes.addressof(desc), stream), "ipe_decode_step")
+    e1.record()
+    torch.cuda.synchronize()
+    untraced = e0.elapsed_time(e1) / 20 * 1000
+    if args.tp:
+        dist.barrier()
+    raw = traced_step(desc, lib.ipe_decode_step_grid(), layers, stream, device)
+    error = nat.device_error()
+    summary = summarize(raw, layers)
+    if args.tp:
+        gathered = [None] * world
+        dist.all_gather_object(gathered, (summary, untraced, error))
+        if rank == 0:
+            for r, (s, u, err) in enumerate(gathered):
+                print(format_summary(s, u, f"rank {r} of {world} (device error {err})"), flush=True)
+        engine.close()
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+    else:
+        print(format_summary(summary, untraced, f"one GPU, batch {args.batch} (device error {error})"), flush=True)
+
+
+if __name__ == "__main__":
+    main()
