@@ -1,5 +1,6 @@
 // The extern "C" boundary: host-side argument checks, then the launchers of the kernel files.
 #include <cstdarg>
+#include <cstdlib>
 #include <cstdio>
 #include <cstring>
 #include <mutex>
@@ -352,8 +353,18 @@ int ipe_prefill_attention(const void* q, const void* k_cache, const void* v_cach
   if (s) return s;
   if (tokens < 1 || tokens > capacity)
     return fail(IPE_ERR_ARGUMENT, "ipe_prefill_attention: tokens %d outside 1..%d", tokens, capacity);
-  return cuda_status(ipe::launch_prefill_attention(q, k_cache, v_cache, out, batch, q_heads, kv_heads, tokens, capacity,
-                                                   as_stream(stream)),
+  if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
+    return fail(IPE_ERR_ARGUMENT, "ipe_prefill_attention: q, caches and out must be 16-byte aligned (TMA)");
+  static const bool mma_sync = [] {  // measurement switch: the earlier mma.sync kernel
+    const char* v = std::getenv("IPE_PREFILL_ATTENTION_MMA");
+    return v && v[0] == '1';
+  }();
+  if (mma_sync)
+    return cuda_status(ipe::launch_prefill_attention(q, k_cache, v_cache, out, batch, q_heads, kv_heads, tokens,
+                                                     capacity, as_stream(stream)),
+                       "ipe_prefill_attention");
+  return cuda_status(ipe::launch_prefill_attention_tc(q, k_cache, v_cache, out, batch, q_heads, kv_heads, tokens,
+                                                      capacity, device_error_word(), as_stream(stream)),
                      "ipe_prefill_attention");
 }
 

@@ -67,6 +67,8 @@ cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, c
                                           const void* sin_t, const int64_t* state, int start, void* k_cache,
                                           void* v_cache, void* out, int batch, int q_heads, int kv_heads, int capacity,
                                           float eps, void* workspace, int* err, cudaStream_t stream);
+cudaError_t launch_prefill_attention_tc(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
+                                        int kv_heads, int tokens, int capacity, int* err, cudaStream_t stream);
 cudaError_t launch_prefill_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                      int kv_heads, int tokens, int capacity, cudaStream_t stream);
 

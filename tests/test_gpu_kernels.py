@@ -372,7 +372,8 @@ def test_fused_decode_attention_matches_the_unfused_ops(batch, hq, hkv, pos, cap
 
 @pytest.mark.parametrize(("batch", "hq", "hkv", "tokens", "cap"),
                          [(1, 16, 8, 1, 8), (2, 16, 8, 17, 32), (1, 16, 8, 64, 64), (1, 16, 8, 65, 80),
-                          (2, 4, 1, 200, 256), (1, 16, 8, 513, 1024), (1, 8, 8, 1024, 1024)])
+                          (2, 4, 1, 200, 256), (1, 16, 8, 513, 1024), (1, 8, 8, 1024, 1024),
+                          (1, 16, 8, 4096, 4352), (3, 8, 2, 300, 320)])
 def test_prefill_attention_matches_fp32(batch, hq, hkv, tokens, cap):
     q = rand((batch, hq, tokens, 128), 33)
     k = torch.full((batch, hkv, cap, 128), float("nan"), dtype=torch.bfloat16, device=DEV)
