@@ -53,6 +53,9 @@ struct StepArgs {
   unsigned prefetch_bytes;  // how far the L2 prefetch runs ahead of the shared-memory copies
   int evict_first;          // weight copies mark their L2 lines evict-first
   int halves;               // half-row-block units allowed
+  int act_cols;             // without ACT_SMEM: RMS-normalised phases with K <= act_cols still stage in shared memory
+  int bulk_stage;           // with ACT_SMEM: phases without a norm stage their rows by bulk copies (batch > 1)
+  int pair_halves;          // one-GPU step: a ring slot carries two half tiles (t and t + 4) of a half unit
   float* cta_records;       // [grid][batch][IPE_PARTIAL_WORDS]: each CTA's merge of its LM-head records
   // tensor parallelism (d.tp_world > 1): byte offsets in a communication region
   size_t recv_x;            // [2 slots][world][batch][hidden / 16][8 lines] parts of o_proj / down_proj
@@ -340,12 +343,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   const int B = d.batch, H = d.hidden, I = d.intermediate;
   const int Q = d.q_heads * 128, QKV = (d.q_heads + 2 * d.kv_heads) * 128;
   const int G_ = static_cast<int>(gridDim.x);
+  const bool pair_halves = !TP && a.pair_halves != 0;
 
+  __shared__ uint64_t stage_bar;  // completion of the bulk copies that stage activation rows
   if (threadIdx.x == 0) {
     for (int s = 0; s < kConsumers * S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
+    mbar_init(&stage_bar, 1);
     *abort_smem = 0;
     fence_barrier_init();
   }
@@ -451,23 +457,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
         const int rb = ph.half ? main_walk.unit >> 1 : main_walk.unit;
         const unsigned char* src = ph.tiles + static_cast<int64_t>(rb) * ph.ku * kTileBytes +
                                    (ph.half ? (main_walk.unit & 1) * (kTileBytes / 2) : 0);
-        for (int t0 = 0; t0 < ph.ku && ok; t0 += kConsumers) {
+        // a paired half unit fills each slot with the half tiles t and t + 4 of its warp
+        const bool pair = pair_halves && ph.half;
+        for (int t0 = 0; t0 < ph.ku && ok; t0 += pair ? 2 * kConsumers : kConsumers) {
 #pragma unroll
           for (int w = 0; w < kConsumers; ++w) {
             const int t = t0 + w;
             if (t >= ph.ku || !ok) continue;
+            const bool two = pair && t + kConsumers < ph.ku;
             const int slot = w * S + sc[w].slot;
             if (sc[w].fill > 0 && !mbar_wait(&empty[slot], (sc[w].fill - 1) & 1, a.err)) {
               ok = false;
               continue;
             }
-            mbar_expect_tx(&full[slot], bytes);
-            if (a.evict_first)
-              bulk_copy_hint(ring_base + slot * kTileBytes, src + static_cast<int64_t>(t) * kTileBytes, bytes,
-                             &full[slot], policy);
-            else
-              bulk_copy(ring_base + slot * kTileBytes, src + static_cast<int64_t>(t) * kTileBytes, bytes,
-                        &full[slot]);
+            mbar_expect_tx(&full[slot], two ? 2 * bytes : bytes);
+#pragma unroll
+            for (int p = 0; p < 2; ++p) {
+              if (p == 1 && !two) break;
+              const uint32_t dst = ring_base + slot * kTileBytes + p * bytes;
+              const unsigned char* from = src + static_cast<int64_t>(t + p * kConsumers) * kTileBytes;
+              if (a.evict_first) bulk_copy_hint(dst, from, bytes, &full[slot], policy);
+              else bulk_copy(dst, from, bytes, &full[slot]);
+            }
             sc[w].advance(S);
           }
         }
@@ -526,10 +537,49 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   }
   if (!phase_end(true)) return;
 
+  // Whether a phase of reduction width K keeps its activation rows in shared memory: always with
+  // ACT_SMEM; otherwise (a batch whose widest rows do not fit) an RMS-normalised phase whose K fits
+  // in the scratch (measured at batch 16: staging beats per-tile normalisation there, while the
+  // phases without a norm are faster reading their activations from L2 tile by tile).
+  auto act_in_smem = [&](int K, bool normed) -> bool { return ACT_SMEM || (normed && K <= a.act_cols); };
+
+  // Stage the B activation rows (row b at src + b * cols, no norm) in shared memory (rows of
+  // cols + kPad) with one bulk copy per row, all on one mbarrier, so the batch costs one round trip
+  // instead of one per row per warp. Callers have synchronised the consumer warps since the last
+  // reads of xs; returns with them synchronised again. A copy that never lands sets the device
+  // error and aborts the step. (Measured: with a norm, the per-lane loads of stage_rows, which
+  // fetch rows and weights together, stay faster.)
+  unsigned stage_parity = 0;
+  auto stage_bulk = [&](const bf16* src, int cols) {
+    const int64_t src_stride = cols;
+    const int xs_cols = cols;
+    if (tid == 0) {
+      // generic writes of xs (this CTA) and of src (every CTA) come before the async-proxy copies
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      const uint32_t bytes = static_cast<uint32_t>(cols) * 2u;
+      mbar_expect_tx(&stage_bar, bytes * static_cast<uint32_t>(B));
+      for (int b = 0; b < B; ++b)
+        bulk_copy(smem_addr(xs + b * (xs_cols + kPad)), src + b * src_stride, bytes, &stage_bar);
+    }
+    if (!mbar_wait(&stage_bar, stage_parity, a.err)) {
+      atomicExch(&a.grid_bar[1], 1u);  // every CTA leaves at its next barrier
+      *abort_smem = 1;
+    }
+    stage_parity ^= 1u;
+    consumers_sync();
+  };
+
   // Stage the activation rows of a phase (optionally RMS-normalised) in shared memory; without
   // shared staging only the RMS scales are kept and tiles read activations from global memory.
   auto stage = [&](const bf16* src, const bf16* norm_w, int K) {
-    stage_rows(src, K, norm_w, d.eps, B, K, xs, K + kPad, rstd, cw, kConsumers, lane, ACT_SMEM);
+    if (ACT_SMEM && a.bulk_stage && !norm_w) {
+      stage_bulk(src, K);
+      mark(2);
+      return;
+    }
+    stage_rows(src, K, norm_w, d.eps, B, K, xs, K + kPad, rstd, cw, kConsumers, lane,
+               act_in_smem(K, norm_w != nullptr));
     consumers_sync();
     mark(2);
   };
@@ -578,9 +628,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   auto run_phase = [&](auto epi_tag, const PhaseShape& ph, const bf16* src, const bf16* norm_w, int K,
                        const EpilogueArgs& ea) -> bool {
     constexpr int EPI = decltype(epi_tag)::value;
+    const bool smem_act = act_in_smem(K, norm_w != nullptr);
     float my_rstd[NT];
 #pragma unroll
-    for (int j = 0; j < NT; ++j) my_rstd[j] = (!ACT_SMEM && norm_w && 8 * j + g < B) ? rstd[8 * j + g] : 1.f;
+    for (int j = 0; j < NT; ++j) my_rstd[j] = (!smem_act && norm_w && 8 * j + g < B) ? rstd[8 * j + g] : 1.f;
     bool ok = true, first = true;
     for (int u = first_unit(cursor); u < ph.units; u += G_) {
       float acc[2][NT][4];
@@ -588,47 +639,59 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int j = 0; j < NT; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0.f;
-      for (int tt = cw; tt < ph.ku && ok; tt += kConsumers) {
-        const int slot = cw * S + mine.slot;
-        const int k0 = tt * kTileK;
-        uint4 xv[4][NT];
+      {
+        // a paired half unit's slot holds this warp's half tiles tt and tt + 4 (the producer's pairing)
+        const bool pair = pair_halves && ph.half;
+        for (int tt = cw; tt < ph.ku && ok; tt += pair ? 2 * kConsumers : kConsumers) {
+          const int slot = cw * S + mine.slot;
+          const uint32_t base = smem_addr(ring + slot * kTileBytes);
+          const int parts = pair && tt + kConsumers < ph.ku ? 2 : 1;
+#pragma unroll 1
+          for (int p = 0; p < parts; ++p) {
+            const int k0 = (tt + p * kConsumers) * kTileK;
+            uint4 xv[4][NT];
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
+            for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int j = 0; j < NT; ++j) {
-            const int b = 8 * j + g;
-            const int kk = k0 + c * 32 + 8 * t;
-            if (b >= B) {
-              xv[c][j] = make_uint4(0, 0, 0, 0);
-            } else if constexpr (ACT_SMEM) {
-              xv[c][j] = *reinterpret_cast<const uint4*>(xs + b * (K + kPad) + kk);
-            } else {
-              uint4 raw = ldcg16(src + static_cast<int64_t>(b) * K + kk);
-              if (norm_w) {
-                float f[8], wf[8];
-                unpack8(raw, f);
-                unpack8(ldg16(norm_w + kk), wf);
+              for (int j = 0; j < NT; ++j) {
+                const int b = 8 * j + g;
+                const int kk = k0 + c * 32 + 8 * t;
+                if (b >= B) {
+                  xv[c][j] = make_uint4(0, 0, 0, 0);
+                } else if (smem_act) {
+                  xv[c][j] = *reinterpret_cast<const uint4*>(xs + b * (K + kPad) + kk);
+                } else {
+                  uint4 raw = ldcg16(src + static_cast<int64_t>(b) * K + kk);
+                  if (norm_w) {
+                    float f[8], wf[8];
+                    unpack8(raw, f);
+                    unpack8(ldg16(norm_w + kk), wf);
 #pragma unroll
-                for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * my_rstd[j]);
-                raw = pack8(f);
+                    for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * my_rstd[j]);
+                    raw = pack8(f);
+                  }
+                  xv[c][j] = raw;
+                }
               }
-              xv[c][j] = raw;
+            if (p == 0) {
+              if (!mbar_wait(&full[slot], mine.fill & 1, a.err)) {
+                ok = false;
+                break;
+              }
+              if (trace) {
+                if (first) mark(3);
+                mark(4);
+                first = false;
+              }
             }
+            if (ph.half) consume_half<NT>(acc, base + p * (kTileBytes / 2), xv, g, t);
+            else consume_tile<NT>(acc, base, xv, g, t);
           }
-        if (!mbar_wait(&full[slot], mine.fill & 1, a.err)) {
-          ok = false;
-          break;
+          if (!ok) break;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&empty[slot]);
+          mine.advance(S);
         }
-        if (trace) {
-          if (first) mark(3);
-          mark(4);
-          first = false;
-        }
-        if (ph.half) consume_half<NT>(acc, smem_addr(ring + slot * kTileBytes), xv, g, t);
-        else consume_tile<NT>(acc, smem_addr(ring + slot * kTileBytes), xv, g, t);
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        mine.advance(S);
       }
       if (ph.half) {  // the two column chains of a half unit
 #pragma unroll
@@ -890,12 +953,14 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // 512-token context: these defaults gave the shortest step): ring slots per consumer warp
 // (IPE_STEP_SLOTS, 4), the L2 prefetch distance per CTA in KB (IPE_STEP_PREFETCH_KB, 128; larger
 // distances lengthened the latency-bound phases), weight copies marked L2 evict-first
-// (IPE_STEP_EVICT_FIRST, 1), and half-row-block units (IPE_STEP_HALF, 1).
+// (IPE_STEP_EVICT_FIRST, 1), half-row-block units (IPE_STEP_HALF, 1), and two half tiles per ring
+// slot in half-unit phases (IPE_STEP_PAIR, 1: twice the bytes in flight per slot).
 struct StepTuning {
   int slots = 4;
   unsigned prefetch_kb = 128;
   int evict_first = 1;
   int halves = 1;
+  int pair = 1;
 };
 
 const StepTuning& tuning() {
@@ -905,6 +970,7 @@ const StepTuning& tuning() {
     if (const char* v = std::getenv("IPE_STEP_PREFETCH_KB")) r.prefetch_kb = static_cast<unsigned>(std::atoi(v));
     if (const char* v = std::getenv("IPE_STEP_EVICT_FIRST")) r.evict_first = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_HALF")) r.halves = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_PAIR")) r.pair = std::atoi(v);
     return r;
   }();
   return t;
@@ -963,15 +1029,26 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   const size_t act = static_cast<size_t>(d.batch) *
                      (std::max(std::max(d.hidden, d.intermediate), d.q_heads * 128) + kPad) * 2;
   const size_t attn = attn_bytes(group);
-  // Activations stay in shared memory when that leaves room for 4 slots per consumer warp.
+  // Activations stay in shared memory when that leaves room for 4 slots per consumer warp. When
+  // the widest rows do not fit (a larger batch), the RMS-normalised phases (QKV, gate/up, the LM
+  // head; reduction width `hidden`) still stage theirs if those fit.
   const bool act_smem = fixed_smem(nt, 4) + std::max(act, attn) <= kSmemMax;
-  const size_t scratch = act_smem ? std::max(act, attn) : attn;
+  const size_t act_h = static_cast<size_t>(d.batch) * (d.hidden + kPad) * 2;
+  const bool act_h_smem = !act_smem && fixed_smem(nt, 4) + std::max(act_h, attn) <= kSmemMax;
+  const size_t scratch = act_smem ? std::max(act, attn) : act_h_smem ? std::max(act_h, attn) : attn;
+  a.act_cols = act_h_smem ? d.hidden : 0;
+  // Bulk staging copies whole rows of the attention output and the SiLU product: 16-byte aligned
+  // buffers and widths. One row is staged by the per-lane loads (a single round trip either way).
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  a.bulk_stage = d.batch > 1 && d.tp_world <= 1 && aligned(d.attn) && aligned(d.act) && d.intermediate % 8 == 0 &&
+                 (d.q_heads * 128) % 8 == 0;
   int slots = std::min(kMaxSlotsPerWarp, std::max(2, tuning().slots));
   while (slots > 2 && fixed_smem(nt, slots) + scratch > kSmemMax) --slots;
   a.slots = slots;
   a.prefetch_bytes = tuning().prefetch_kb * 1024u;
   a.evict_first = tuning().evict_first;
   a.halves = tuning().halves;
+  a.pair_halves = tuning().pair;
   const size_t smem = fixed_smem(nt, slots) + scratch;
   if (smem > kSmemMax) {
     *message = "decode-step scratch does not fit in shared memory";

@@ -248,8 +248,11 @@ def test_decode_steps_never_synchronize_or_grow_the_allocator(models):
 @pytest.mark.parametrize(("name", "batch", "length", "prompt"), [
     ("small", 2, 20, 6),
     ("qwen3-1.7b-2layer", 1, 700, 694),   # one row: 11 attention splits merged, half-tile o/down units
-    ("qwen3-1.7b-2layer", 4, 300, 296),   # 4 rows: activations staged in shared memory, 4 splits
-    ("qwen3-1.7b-2layer", 16, 300, 296),  # 16 rows: two MMA column tiles, activations read from L2,
+    ("qwen3-1.7b-2layer", 4, 300, 296),   # 4 rows: activations staged in shared memory (o_proj and
+                                          # down_proj rows by bulk copies), 4 splits
+    ("qwen3-1.7b-2layer", 8, 300, 296),   # 8 rows: the normalised rows (QKV, gate/up, LM head) staged
+                                          # in shared memory, o_proj / down_proj reading theirs from L2
+    ("qwen3-1.7b-2layer", 16, 300, 296),  # 16 rows: two MMA column tiles, the same split staging,
                                           # one attention split streaming many 32-key sub-chunks
 ])
 def test_one_kernel_step_agrees_with_the_per_operator_kernels(models, monkeypatch, name, batch, length, prompt):
