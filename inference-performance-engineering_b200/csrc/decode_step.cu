@@ -283,6 +283,38 @@ __device__ __noinline__ MergedRecords tp_merge_records(const StepArgs& a, const 
   return m;
 }
 
+// This lane's activation vectors for the tile whose columns start at k0 (batch columns 8j + g):
+// from the staged rows xs (row stride K + pad) or, without staging, from src in global memory with
+// the RMS scale and norm weight applied (the reference's two roundings). Rows past the batch are 0.
+template <int NT>
+__device__ __forceinline__ void load_activations(uint4 (&xv)[4][NT], int k0, bool staged, const bf16* xs,
+                                                 const bf16* src, const bf16* norm_w, const float (&rstd)[NT], int K,
+                                                 int pad, int B, int g, int t) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c)
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      const int b = 8 * j + g;
+      const int kk = k0 + c * 32 + 8 * t;
+      if (b >= B) {
+        xv[c][j] = make_uint4(0, 0, 0, 0);
+      } else if (staged) {
+        xv[c][j] = *reinterpret_cast<const uint4*>(xs + b * (K + pad) + kk);
+      } else {
+        uint4 raw = ldcg16(src + static_cast<int64_t>(b) * K + kk);
+        if (norm_w) {
+          float f[8], wf[8];
+          unpack8(raw, f);
+          unpack8(ldg16(norm_w + kk), wf);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * rstd[j]);
+          raw = pack8(f);
+        }
+        xv[c][j] = raw;
+      }
+    }
+}
+
 // First unit of this CTA in a phase that starts dealing at `cursor`.
 __device__ __forceinline__ int first_unit(int cursor) {
   const int g = static_cast<int>(gridDim.x);
@@ -645,49 +677,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
         for (int tt = cw; tt < ph.ku && ok; tt += pair ? 2 * kConsumers : kConsumers) {
           const int slot = cw * S + mine.slot;
           const uint32_t base = smem_addr(ring + slot * kTileBytes);
-          const int parts = pair && tt + kConsumers < ph.ku ? 2 : 1;
-#pragma unroll 1
-          for (int p = 0; p < parts; ++p) {
-            const int k0 = (tt + p * kConsumers) * kTileK;
-            uint4 xv[4][NT];
-#pragma unroll
-            for (int c = 0; c < 4; ++c)
-#pragma unroll
-              for (int j = 0; j < NT; ++j) {
-                const int b = 8 * j + g;
-                const int kk = k0 + c * 32 + 8 * t;
-                if (b >= B) {
-                  xv[c][j] = make_uint4(0, 0, 0, 0);
-                } else if (smem_act) {
-                  xv[c][j] = *reinterpret_cast<const uint4*>(xs + b * (K + kPad) + kk);
-                } else {
-                  uint4 raw = ldcg16(src + static_cast<int64_t>(b) * K + kk);
-                  if (norm_w) {
-                    float f[8], wf[8];
-                    unpack8(raw, f);
-                    unpack8(ldg16(norm_w + kk), wf);
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * my_rstd[j]);
-                    raw = pack8(f);
-                  }
-                  xv[c][j] = raw;
-                }
-              }
-            if (p == 0) {
-              if (!mbar_wait(&full[slot], mine.fill & 1, a.err)) {
-                ok = false;
-                break;
-              }
-              if (trace) {
-                if (first) mark(3);
-                mark(4);
-                first = false;
-              }
-            }
-            if (ph.half) consume_half<NT>(acc, base + p * (kTileBytes / 2), xv, g, t);
-            else consume_tile<NT>(acc, base, xv, g, t);
+          uint4 xv[4][NT];
+          load_activations<NT>(xv, tt * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
+          if (!mbar_wait(&full[slot], mine.fill & 1, a.err)) {
+            ok = false;
+            break;
           }
-          if (!ok) break;
+          if (trace) {
+            if (first) mark(3);
+            mark(4);
+            first = false;
+          }
+          if (ph.half) consume_half<NT>(acc, base, xv, g, t);
+          else consume_tile<NT>(acc, base, xv, g, t);
+          if (pair && tt + kConsumers < ph.ku) {
+            load_activations<NT>(xv, (tt + kConsumers) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
+            consume_half<NT>(acc, base + kTileBytes / 2, xv, g, t);
+          }
           __syncwarp();
           if (lane == 0) mbar_arrive(&empty[slot]);
           mine.advance(S);
