@@ -604,7 +604,51 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
 
   // Stage the activation rows of a phase (optionally RMS-normalised) in shared memory; without
   // shared staging only the RMS scales are kept and tiles read activations from global memory.
+  // One RMS-normalised row (batch 1, K <= 2048) staged by all four consumer warps, two 16-byte
+  // vectors and their weights per lane, the warps' sums of squares added in warp order through
+  // shared memory: the one-warp path of stage_rows leaves three warps idle on the critical path.
+  auto stage_one_normed = [&](const bf16* src, const bf16* norm_w, int K) {
+    const int chunks = K / 8;
+    uint4 v[2], w[2];
+    float ss = 0.f;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = u * kCThreads + tid;
+      v[u] = c < chunks ? ldcg16(src + c * 8) : make_uint4(0, 0, 0, 0);
+      w[u] = c < chunks ? ldg16(norm_w + c * 8) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float f[8];
+      unpack8(v[u], f);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += f[e] * f[e];
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red_ss[cw] = ss;
+    consumers_sync();
+    const float r = rsqrtf((red_ss[0] + red_ss[1] + red_ss[2] + red_ss[3]) / static_cast<float>(K) + d.eps);
+    if (tid == 0) rstd[0] = r;
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = u * kCThreads + tid;
+      if (c >= chunks) continue;
+      float f[8], wf[8];
+      unpack8(v[u], f);
+      unpack8(w[u], wf);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) f[e] = wf[e] * bf16_round(f[e] * r);
+      *reinterpret_cast<uint4*>(xs + c * 8) = pack8(f);
+    }
+  };
+
   auto stage = [&](const bf16* src, const bf16* norm_w, int K) {
+    if (!TP && B == 1 && norm_w && K <= 2 * 8 * kCThreads && K % 8 == 0 && act_in_smem(K, true)) {
+      stage_one_normed(src, norm_w, K);
+      consumers_sync();
+      mark(2);
+      return;
+    }
     if (ACT_SMEM && a.bulk_stage && !norm_w) {
       stage_bulk(src, K);
       mark(2);
