@@ -56,6 +56,7 @@ struct StepArgs {
   int act_cols;             // without ACT_SMEM: RMS-normalised phases with K <= act_cols still stage in shared memory
   int bulk_stage;           // with ACT_SMEM: phases without a norm stage their rows by bulk copies (batch > 1)
   int pair_halves;          // one-GPU step: a ring slot carries two half tiles (t and t + 4) of a half unit
+  unsigned xres_off;        // bulk staging: byte offset from the scratch of a copy of the residual rows x (0: none)
   float* cta_records;       // [grid][batch][IPE_PARTIAL_WORDS]: each CTA's merge of its LM-head records
   // tensor parallelism (d.tp_world > 1): byte offsets in a communication region
   size_t recv_x;            // [2 slots][world][batch][hidden / 16][8 lines] parts of o_proj / down_proj
@@ -368,6 +369,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   int* abort_smem = reinterpret_cast<int*>(rstd + 16);
   float* red = reinterpret_cast<float*>(abort_smem + 4);  // [kConsumers][32][8 * NT]
   float* scratch = red + kConsumers * 32 * 8 * NT;        // activations or attention scratch
+  bf16* xres = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(scratch) + a.xres_off);  // if xres_off
   bf16* xs = reinterpret_cast<bf16*>(scratch);
 
   const ipe_decode_step_desc& d = a.d;
@@ -582,7 +584,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   // error and aborts the step. (Measured: with a norm, the per-lane loads of stage_rows, which
   // fetch rows and weights together, stay faster.)
   unsigned stage_parity = 0;
-  auto stage_bulk = [&](const bf16* src, int cols) {
+  // With res (the residual rows x of an o_proj / down_proj phase) and a residual copy in shared
+  // memory (xres), those rows arrive on the same mbarrier, so the phase's residual epilogues read
+  // shared memory instead of making an L2 round trip per unit.
+  auto stage_bulk = [&](const bf16* src, int cols, const bf16* res) {
     const int64_t src_stride = cols;
     const int xs_cols = cols;
     if (tid == 0) {
@@ -590,9 +595,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       asm volatile("fence.proxy.async.global;" ::: "memory");
       const uint32_t bytes = static_cast<uint32_t>(cols) * 2u;
-      mbar_expect_tx(&stage_bar, bytes * static_cast<uint32_t>(B));
+      const uint32_t res_bytes = res ? static_cast<uint32_t>(H) * 2u : 0u;
+      mbar_expect_tx(&stage_bar, (bytes + res_bytes) * static_cast<uint32_t>(B));
       for (int b = 0; b < B; ++b)
         bulk_copy(smem_addr(xs + b * (xs_cols + kPad)), src + b * src_stride, bytes, &stage_bar);
+      if (res)
+        for (int b = 0; b < B; ++b) bulk_copy(smem_addr(xres + b * H), res + b * H, res_bytes, &stage_bar);
     }
     if (!mbar_wait(&stage_bar, stage_parity, a.err)) {
       atomicExch(&a.grid_bar[1], 1u);  // every CTA leaves at its next barrier
@@ -642,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     }
   };
 
-  auto stage = [&](const bf16* src, const bf16* norm_w, int K) {
+  auto stage = [&](const bf16* src, const bf16* norm_w, int K, const bf16* res = nullptr) {
     if (!TP && B == 1 && norm_w && K <= 2 * 8 * kCThreads && K % 8 == 0 && act_in_smem(K, true)) {
       stage_one_normed(src, norm_w, K);
       consumers_sync();
@@ -650,7 +658,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       return;
     }
     if (ACT_SMEM && a.bulk_stage && !norm_w) {
-      stage_bulk(src, K);
+      stage_bulk(src, K, a.xres_off ? res : nullptr);
       mark(2);
       return;
     }
@@ -801,6 +809,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     return;  // every CTA sees the same position and leaves before the next barrier
   }
   const AttnSplit sp = attn_split(pos, a.max_splits);
+  // o_proj / down_proj epilogues: x += bf16(sum), x read from its shared-memory copy when the
+  // bulk staging brought one
+  EpilogueArgs residual_args{x, H, H, B, nullptr, nullptr, 0.f, 0};
+  if (ACT_SMEM && !TP && a.bulk_stage && a.xres_off != 0) residual_args.res_smem = xres;
 
   for (int layer = 0; layer < d.layers; ++layer) {
     const ipe_layer_desc& L = d.layer_descs[layer];
@@ -847,11 +859,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     }
     if (!phase_end(true)) return;
     // o_proj + residual (tensor parallel: this rank's part, pushed to every rank)
-    stage(attn, nullptr, Q);
+    stage(attn, nullptr, Q, x);
     tp_slot = 0;
     ++tp_epoch;
-    if (!run_phase(EpiResidual{}, phase_shape(layer, 1), attn, nullptr, Q,
-                   EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
+    if (!run_phase(EpiResidual{}, phase_shape(layer, 1), attn, nullptr, Q, residual_args))
       return;
     if (!phase_end(!tp)) return;
     // post-attention RMSNorm + gate/up + SiLU * up (tensor parallel: the residual stream moves back
@@ -867,11 +878,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       return;
     if (!phase_end(true)) return;
     // down_proj + residual (tensor parallel: this rank's part, pushed to every rank)
-    stage(act, nullptr, I);
+    stage(act, nullptr, I, x);
     tp_slot = 1;
     ++tp_epoch;
-    if (!run_phase(EpiResidual{}, phase_shape(layer, 3), act, nullptr, I,
-                   EpilogueArgs{x, H, H, B, nullptr, nullptr, 0.f, 0}))
+    if (!run_phase(EpiResidual{}, phase_shape(layer, 3), act, nullptr, I, residual_args))
       return;
     if (!phase_end(!tp)) return;
   }
@@ -1004,13 +1014,15 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // (IPE_STEP_SLOTS, 4), the L2 prefetch distance per CTA in KB (IPE_STEP_PREFETCH_KB, 128; larger
 // distances lengthened the latency-bound phases), weight copies marked L2 evict-first
 // (IPE_STEP_EVICT_FIRST, 1), half-row-block units (IPE_STEP_HALF, 1), and two half tiles per ring
-// slot in half-unit phases (IPE_STEP_PAIR, 1: twice the bytes in flight per slot).
+// slot in half-unit phases (IPE_STEP_PAIR, 1: twice the bytes in flight per slot), and bulk-copy
+// staging of the o_proj / down_proj rows with the residual rows beside them (IPE_STEP_BULK, 1).
 struct StepTuning {
   int slots = 4;
   unsigned prefetch_kb = 128;
   int evict_first = 1;
   int halves = 1;
   int pair = 1;
+  int bulk = 1;
 };
 
 const StepTuning& tuning() {
@@ -1021,6 +1033,7 @@ const StepTuning& tuning() {
     if (const char* v = std::getenv("IPE_STEP_EVICT_FIRST")) r.evict_first = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_HALF")) r.halves = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_PAIR")) r.pair = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_BULK")) r.bulk = std::atoi(v);
     return r;
   }();
   return t;
@@ -1085,13 +1098,23 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   const bool act_smem = fixed_smem(nt, 4) + std::max(act, attn) <= kSmemMax;
   const size_t act_h = static_cast<size_t>(d.batch) * (d.hidden + kPad) * 2;
   const bool act_h_smem = !act_smem && fixed_smem(nt, 4) + std::max(act_h, attn) <= kSmemMax;
-  const size_t scratch = act_smem ? std::max(act, attn) : act_h_smem ? std::max(act_h, attn) : attn;
+  size_t scratch = act_smem ? std::max(act, attn) : act_h_smem ? std::max(act_h, attn) : attn;
   a.act_cols = act_h_smem ? d.hidden : 0;
   // Bulk staging copies whole rows of the attention output and the SiLU product: 16-byte aligned
-  // buffers and widths. One row is staged by the per-lane loads (a single round trip either way).
+  // buffers and widths.
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  a.bulk_stage = d.batch > 1 && d.tp_world <= 1 && aligned(d.attn) && aligned(d.act) && d.intermediate % 8 == 0 &&
+  a.bulk_stage = tuning().bulk && d.tp_world <= 1 && aligned(d.attn) && aligned(d.act) && d.intermediate % 8 == 0 &&
                  (d.q_heads * 128) % 8 == 0;
+  // The residual rows' shared-memory copy (bulk-staged o_proj / down_proj phases), after the scratch
+  // when that still leaves 4 slots per consumer warp.
+  a.xres_off = 0;
+  const size_t xres_bytes = static_cast<size_t>(d.batch) * d.hidden * 2;
+  const size_t scratch16 = (scratch + 15) / 16 * 16;
+  if (act_smem && a.bulk_stage && aligned(d.x) && d.hidden % 8 == 0 &&
+      fixed_smem(nt, 4) + scratch16 + xres_bytes <= kSmemMax) {
+    a.xres_off = static_cast<unsigned>(scratch16);
+    scratch = scratch16 + xres_bytes;
+  }
   int slots = std::min(kMaxSlotsPerWarp, std::max(2, tuning().slots));
   while (slots > 2 && fixed_smem(nt, slots) + scratch > kSmemMax) --slots;
   a.slots = slots;

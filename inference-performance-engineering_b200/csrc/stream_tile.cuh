@@ -201,6 +201,7 @@ struct EpilogueArgs {
   float temperature;
   uint64_t seed;
   int row_offset = 0;  // logits: global vocabulary ID of row 0 (a vocabulary shard)
+  const bf16* res_smem = nullptr;  // residual: a shared-memory copy of out's rows (row stride out_stride), or null
 };
 
 // Row block rb's outputs from the complete fp32 sums acc (lane layout of mma m16n8: rows
@@ -225,7 +226,10 @@ __device__ __forceinline__ void row_block_epilogue(const float (&acc)[2][NT][4],
           if (b >= B || n >= a.rows) continue;
           bf16* dst = out + b * a.out_stride + n;
           if constexpr (EPI == kGemvStore) *dst = __float2bfloat16_rn(acc[h][j][e]);
-          else *dst = __float2bfloat16_rn(ldcg_bf16(dst) + bf16_round(acc[h][j][e]));
+          else {
+            const float res = a.res_smem ? __bfloat162float(a.res_smem[b * a.out_stride + n]) : ldcg_bf16(dst);
+            *dst = __float2bfloat16_rn(res + bf16_round(acc[h][j][e]));
+          }
         }
     }
   } else if constexpr (EPI == kGemvSiluMul) {
