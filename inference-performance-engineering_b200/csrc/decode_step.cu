@@ -57,6 +57,7 @@ struct StepArgs {
   int bulk_stage;           // with ACT_SMEM: phases without a norm stage their rows by bulk copies (batch > 1)
   int pair_halves;          // one-GPU step: a ring slot carries two half tiles (t and t + 4) of a half unit
   unsigned xres_off;        // bulk staging: byte offset from the scratch of a copy of the residual rows x (0: none)
+  int light_fences;         // grid barrier: acq_rel fence before the arrival, no fence after the acquire load
   float* cta_records;       // [grid][batch][IPE_PARTIAL_WORDS]: each CTA's merge of its LM-head records
   // tensor parallelism (d.tp_world > 1): byte offsets in a communication region
   size_t recv_x;            // [2 slots][world][batch][hidden / 16][8 lines] parts of o_proj / down_proj
@@ -80,7 +81,9 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
   consumers_sync();
   if (tid == 0) {
     if (tr) tr[0] = globaltimer_ns();
-    __threadfence();
+    // release: the consumer warps' writes (ordered before by the named barrier) before the arrival
+    if (a.light_fences) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    else __threadfence();
     atomicAdd(&a.grid_bar[0], 1u);
     const unsigned target = index * gridDim.x;
     uint64_t start = 0;
@@ -102,7 +105,9 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
       }
       __nanosleep(64);
     }
-    __threadfence();
+    // the acquire load that saw the count already orders this CTA's later reads (through the
+    // named barrier below); the full fence is kept as the measured alternative
+    if (!a.light_fences) __threadfence();
     if (tr) tr[1] = globaltimer_ns();
   }
   consumers_sync();
@@ -1015,7 +1020,8 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // distances lengthened the latency-bound phases), weight copies marked L2 evict-first
 // (IPE_STEP_EVICT_FIRST, 1), half-row-block units (IPE_STEP_HALF, 1), and two half tiles per ring
 // slot in half-unit phases (IPE_STEP_PAIR, 1: twice the bytes in flight per slot), and bulk-copy
-// staging of the o_proj / down_proj rows with the residual rows beside them (IPE_STEP_BULK, 1).
+// staging of the o_proj / down_proj rows with the residual rows beside them (IPE_STEP_BULK, 1), and
+// the grid barrier's lighter fences (IPE_STEP_LIGHT_FENCES, 1).
 struct StepTuning {
   int slots = 4;
   unsigned prefetch_kb = 128;
@@ -1023,6 +1029,7 @@ struct StepTuning {
   int halves = 1;
   int pair = 1;
   int bulk = 1;
+  int light_fences = 1;
 };
 
 const StepTuning& tuning() {
@@ -1034,6 +1041,7 @@ const StepTuning& tuning() {
     if (const char* v = std::getenv("IPE_STEP_HALF")) r.halves = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_PAIR")) r.pair = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_BULK")) r.bulk = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_LIGHT_FENCES")) r.light_fences = std::atoi(v);
     return r;
   }();
   return t;
@@ -1122,6 +1130,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   a.evict_first = tuning().evict_first;
   a.halves = tuning().halves;
   a.pair_halves = tuning().pair;
+  a.light_fences = tuning().light_fences;
   const size_t smem = fixed_smem(nt, slots) + scratch;
   if (smem > kSmemMax) {
     *message = "decode-step scratch does not fit in shared memory";
