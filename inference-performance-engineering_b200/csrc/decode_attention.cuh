@@ -320,18 +320,23 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
       __stcg(rec + 129, s.stat[2 * g + 1]);
     }
   }
-  // Arrival: the last split of this (row, KV head) merges every split.
-  __threadfence();
+  // Arrival: the last split of this (row, KV head) merges every split. The records written by
+  // every thread are ordered before thread 0's acq_rel fence by the barrier (release); the last
+  // arriver's fence after its counter update orders the merge's reads after it (acquire), and the
+  // barrier passes that on to the other threads.
   attn_sync();
   if (tid == 0) {
     int* counter = a.counters + b * a.kv_heads + kvh;
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
     const int prior = atomicAdd(counter, 1);
     *s.last = prior == sp.splits - 1;
-    if (*s.last) *counter = 0;
+    if (*s.last) {
+      *counter = 0;
+      asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    }
   }
   attn_sync();
   if (!*s.last) return;
-  __threadfence();
   // Per head (one lane per split): weights exp(m_s - M) / L, then every thread sums its dims.
   for (int g = warp; g < G; g += kAttnThreads / 32) {
     const float* base = a.records + (static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * kAttnSplitsMax * kAttnRecord;
