@@ -58,6 +58,7 @@ struct StepArgs {
   int pair_halves;          // one-GPU step: a ring slot carries two half tiles (t and t + 4) of a half unit
   unsigned xres_off;        // bulk staging: byte offset from the scratch of a copy of the residual rows x (0: none)
   int light_fences;         // grid barrier: acq_rel fence before the arrival, no fence after the acquire load
+  int overlap_epilogue;     // warps 1-3 start the next unit while warp 0 runs this unit's epilogue
   float* cta_records;       // [grid][batch][IPE_PARTIAL_WORDS]: each CTA's merge of its LM-head records
   // tensor parallelism (d.tp_world > 1): byte offsets in a communication region
   size_t recv_x;            // [2 slots][world][batch][hidden / 16][8 lines] parts of o_proj / down_proj
@@ -372,8 +373,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   uint64_t* empty = full + kMaxStages;
   float* rstd = reinterpret_cast<float*>(empty + kMaxStages);  // [16]
   int* abort_smem = reinterpret_cast<int*>(rstd + 16);
-  float* red = reinterpret_cast<float*>(abort_smem + 4);  // [kConsumers][32][8 * NT]
-  float* scratch = red + kConsumers * 32 * 8 * NT;        // activations or attention scratch
+  float* red = reinterpret_cast<float*>(abort_smem + 4);  // [2 units][kConsumers][32][8 * NT]
+  float* scratch = red + 2 * kConsumers * 32 * 8 * NT;    // activations or attention scratch
   bf16* xres = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(scratch) + a.xres_off);  // if xres_off
   bf16* xs = reinterpret_cast<bf16*>(scratch);
 
@@ -535,6 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   // phase ends so far (each a grid barrier, or in tensor-parallel steps after a row-parallel phase
   // the end of this CTA's pushes), and grid barriers so far
   unsigned barrier_index = 0, syncs = 0;
+  unsigned red_flip = 0;  // units consumed so far: which partial-sum buffer the next one uses
   int64_t* state = d.state;
   uint64_t* trace = d.trace ? d.trace + static_cast<int64_t>(blockIdx.x) * IPE_TRACE_WORDS(d.layers) : nullptr;
   if (trace && tid == 0) trace[0] = globaltimer_ns();
@@ -762,8 +764,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
 #pragma unroll
           for (int e = 0; e < 4; ++e) acc[0][j][e] += acc[1][j][e];
       }
-      // Fixed-order reduction of the warps' partial sums, then the epilogue by warp 0.
-      float* part = red + (cw * 32 + lane) * 8 * NT;
+      // Fixed-order reduction of the warps' partial sums, then the epilogue by warp 0. Units
+      // alternate between two partial-sum buffers, so with overlap_epilogue warps 1-3 go on to the
+      // next unit's tiles while warp 0 finishes this one: the barrier after the next unit's
+      // partials is the one that orders warp 0's reads of this buffer before its reuse.
+      float* red_u = red + (red_flip++ & 1u) * (kConsumers * 32 * 8 * NT);
+      float* part = red_u + (cw * 32 + lane) * 8 * NT;
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -774,7 +780,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       if (cw == 0) {
 #pragma unroll
         for (int w = 1; w < kConsumers; ++w) {
-          const float* other = red + (w * 32 + lane) * 8 * NT;
+          const float* other = red_u + (w * 32 + lane) * 8 * NT;
 #pragma unroll
           for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -792,9 +798,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
           row_block_epilogue<EPI, NT>(acc, u, lane, ea);
         }
       }
-      consumers_sync();
+      if (!a.overlap_epilogue) consumers_sync();
       if (!ok) return false;
     }
+    if (a.overlap_epilogue) consumers_sync();  // warp 0's last epilogue of the phase is done
     cursor = (cursor + ph.units) % G_;
     return true;
   };
@@ -1021,7 +1028,8 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // (IPE_STEP_EVICT_FIRST, 1), half-row-block units (IPE_STEP_HALF, 1), and two half tiles per ring
 // slot in half-unit phases (IPE_STEP_PAIR, 1: twice the bytes in flight per slot), and bulk-copy
 // staging of the o_proj / down_proj rows with the residual rows beside them (IPE_STEP_BULK, 1), and
-// the grid barrier's lighter fences (IPE_STEP_LIGHT_FENCES, 1).
+// the grid barrier's lighter fences (IPE_STEP_LIGHT_FENCES, 1), and the unit epilogue overlapped with
+// the next unit's tiles (IPE_STEP_OVERLAP, 1).
 struct StepTuning {
   int slots = 4;
   unsigned prefetch_kb = 128;
@@ -1030,6 +1038,7 @@ struct StepTuning {
   int pair = 1;
   int bulk = 1;
   int light_fences = 1;
+  int overlap_epilogue = 1;
 };
 
 const StepTuning& tuning() {
@@ -1042,6 +1051,7 @@ const StepTuning& tuning() {
     if (const char* v = std::getenv("IPE_STEP_PAIR")) r.pair = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_BULK")) r.bulk = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_LIGHT_FENCES")) r.light_fences = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_OVERLAP")) r.overlap_epilogue = std::atoi(v);
     return r;
   }();
   return t;
@@ -1049,7 +1059,7 @@ const StepTuning& tuning() {
 
 size_t fixed_smem(int nt, int slots) {
   return 1024 + static_cast<size_t>(kConsumers) * slots * kTileBytes + 2 * kMaxStages * 8 + 16 * 4 + 16 +
-         static_cast<size_t>(kConsumers) * 32 * 8 * nt * 4;
+         2 * static_cast<size_t>(kConsumers) * 32 * 8 * nt * 4;
 }
 
 size_t attn_bytes(int group) {
@@ -1131,6 +1141,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   a.halves = tuning().halves;
   a.pair_halves = tuning().pair;
   a.light_fences = tuning().light_fences;
+  a.overlap_epilogue = tuning().overlap_epilogue;
   const size_t smem = fixed_smem(nt, slots) + scratch;
   if (smem > kSmemMax) {
     *message = "decode-step scratch does not fit in shared memory";
