@@ -182,6 +182,8 @@ int ipe_sample_logits(const float* logits, int64_t rows, int vocab, float temper
  * j / (q_heads / kv_heads)), scale 128^-0.5, fp32 softmax.
  *   q bf16 [batch, q_heads, 128] -> out bf16 [batch, q_heads * 128]
  * workspace: ipe_decode_attention_workspace(batch, q_heads, capacity) bytes of device memory.
+ * A device state whose position lies outside 0..capacity-1 makes the kernels read and write
+ * nothing and sets the device error word to 2 (ipe_device_error).
  * Replaces ops.attention for decode steps (src/ipe/ops.py:78-101, causal=False). */
 int ipe_decode_attention(const void* q, const void* k_cache, const void* v_cache, void* out,
                          int batch, int q_heads, int kv_heads, int capacity, int length,
@@ -211,6 +213,8 @@ size_t ipe_decode_attention_qkv_workspace(int batch, int q_heads, int kv_heads, 
  * in device memory, which every GPU that loads the library holds until the process exits.
  * Limit: ipe_decode_attention_workspace(batch, q_heads, capacity) must be <= 2 MiB (for 16 query
  * heads: batch x capacity up to about 8,000 positions), else IPE_ERR_UNSUPPORTED and nothing runs.
+ * A device state position outside 0..capacity-1 is handled as by ipe_decode_attention: nothing
+ * is read or written and the device error word reads 2.
  * The first call on each device looks up the array's device address (cudaGetSymbolAddress, with
  * that device current); make that first call before any stream capture. All calls share the one
  * array and it keeps the last call's contents; nothing in it needs clearing, because a call only
@@ -333,7 +337,7 @@ typedef struct {
    * intermediate and vocab (LM-head rows, from vocab_offset) are then this rank's shard; the
    * weights, caches and tiles above are the shard's. o_proj and down_proj push fp32 parts into
    * every rank's communication region (tp_peers: device array of the tp_world region pointers,
-   * ipe_decode_step_comm_bytes each, zero-filled once) as flagged 16-byte lines, and the next
+   * ipe_decode_step_comm_bytes each, zero-filled once) as flagged 64-bit elements {value, epoch}, and the next
    * phase polls and sums them in rank order; each CTA's merge of its LM-head records goes to
    * every rank the same way and every rank samples the same token. No grid barrier follows a row-parallel phase. x_alt: a
    * second bf16 [batch, hidden] residual buffer. Needs hidden % 512 == 0 and the activations in
@@ -343,6 +347,10 @@ typedef struct {
   void* x_alt;
   int vocab_offset;                  /* first vocabulary ID of this rank's LM-head rows        */
   int vocab_total;                   /* the full vocabulary (token IDs)                         */
+  /* Bound of every spin-wait of the step (grid barriers, shared-memory copies, a peer's parts) in
+   * nanoseconds; 0 means 2 s. A wait that runs out sets device error 3 (ipe_device_error), every
+   * CTA leaves at its next wait, and the step neither samples nor advances state[IPE_STATE_POS]. */
+  int64_t wait_limit_ns;
 } ipe_decode_step_desc;
 
 /* Step trace (when desc.trace is set): CTA c writes globaltimer nanoseconds to

@@ -22,9 +22,15 @@ template <int G>
 __global__ void __launch_bounds__(kThreads) decode_chunk_kernel(const bf16* __restrict__ q, const bf16* __restrict__ kc,
                                                                 const bf16* __restrict__ vc, float* __restrict__ ws,
                                                                 int q_heads, int kv_heads, int capacity, int length_arg,
-                                                                const int64_t* __restrict__ state, int chunks_max) {
+                                                                const int64_t* __restrict__ state, int chunks_max,
+                                                                int* err) {
   const int chunk = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int length = state ? static_cast<int>(state[IPE_STATE_POS]) + 1 : length_arg;
+  // a device position outside the cache: nothing is read or written (the host checks a host length)
+  if (length < 1 || length > capacity) {
+    if (chunk == 0 && kvh == 0 && b == 0 && threadIdx.x == 0) report(err, kErrPositionRange);
+    return;
+  }
   const int key0 = chunk * kChunk;
   if (key0 >= length) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -129,11 +135,12 @@ __global__ void __launch_bounds__(kThreads) decode_chunk_kernel(const bf16* __re
 }
 
 __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __restrict__ ws, bf16* __restrict__ out,
-                                                             int q_heads, int length_arg,
+                                                             int q_heads, int capacity, int length_arg,
                                                              const int64_t* __restrict__ state, int chunks_max) {
   const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int length = state ? static_cast<int>(state[IPE_STATE_POS]) + 1 : length_arg;
-  const int chunks = (length + kChunk - 1) / kChunk;
+  if (length < 1 || length > capacity) return;  // reported by the chunk kernel; the output is left as it was
+  const int chunks = min((length + kChunk - 1) / kChunk, chunks_max);
   const float* base = ws + (static_cast<int64_t>(b) * q_heads + head) * chunks_max * kRecord;
   float m = -INFINITY;
   for (int c = 0; c < chunks; ++c) m = fmaxf(m, base[c * kRecord + 128]);
@@ -167,9 +174,9 @@ __global__ void __launch_bounds__(kAttnThreads) fused_decode_kernel(const FusedA
 
 template <int G>
 void launch_chunks(dim3 grid, const bf16* q, const bf16* k, const bf16* v, float* ws, int q_heads, int kv_heads,
-                   int capacity, int length, const int64_t* state, int chunks_max, cudaStream_t stream) {
+                   int capacity, int length, const int64_t* state, int chunks_max, int* err, cudaStream_t stream) {
   decode_chunk_kernel<G><<<grid, kThreads, 0, stream>>>(q, k, v, ws, q_heads, kv_heads, capacity, length, state,
-                                                        chunks_max);
+                                                        chunks_max, err);
 }
 
 }  // namespace
@@ -178,7 +185,7 @@ int decode_attention_chunk() { return kChunk; }
 
 cudaError_t launch_decode_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                     int kv_heads, int capacity, int length, const int64_t* state, float* ws,
-                                    cudaStream_t stream) {
+                                    int* err, cudaStream_t stream) {
   const int chunks_max = (capacity + kChunk - 1) / kChunk;
   const int group = q_heads / kv_heads;
   const dim3 grid(chunks_max, kv_heads, batch);
@@ -186,16 +193,16 @@ cudaError_t launch_decode_attention(const void* q, const void* k, const void* v,
   auto kk = static_cast<const bf16*>(k);
   auto vv = static_cast<const bf16*>(v);
   switch (group) {
-    case 1: launch_chunks<1>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
-    case 2: launch_chunks<2>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
-    case 4: launch_chunks<4>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
-    case 8: launch_chunks<8>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, stream); break;
+    case 1: launch_chunks<1>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, err, stream); break;
+    case 2: launch_chunks<2>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, err, stream); break;
+    case 4: launch_chunks<4>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, err, stream); break;
+    case 8: launch_chunks<8>(grid, qq, kk, vv, ws, q_heads, kv_heads, capacity, length, state, chunks_max, err, stream); break;
     default: return cudaErrorInvalidValue;
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
-  decode_combine_kernel<<<dim3(q_heads, batch), 128, 0, stream>>>(ws, static_cast<bf16*>(out), q_heads, length, state,
-                                                                   chunks_max);
+  decode_combine_kernel<<<dim3(q_heads, batch), 128, 0, stream>>>(ws, static_cast<bf16*>(out), q_heads, capacity,
+                                                                   length, state, chunks_max);
   return cudaGetLastError();
 }
 

@@ -16,8 +16,8 @@
 //              128^-0.5 scale folded in, P rounded to bf16 into shared memory (the same swizzle
 //              TMA writes), O rescaled in TMEM (tcgen05.ld / st) only when a row's max moved, and
 //              at the end O / l rounded to bf16 to the [batch, tokens, q_heads * 128] output.
-// The arithmetic is the mma.sync kernel's (attention_prefill.cu) with another summation order:
-// fp32 scores, fp32 softmax statistics, bf16 P, fp32 P V accumulation, one rounding of O / l.
+// Arithmetic: fp32 scores, fp32 softmax statistics, bf16 P, fp32 P V accumulation, one rounding
+// of O / l.
 // Query blocks are scheduled heaviest first (the causal work grows with the block index). Every
 // mbarrier wait is bounded; a timeout sets the device error word and the CTA winds down.
 #include "common.cuh"

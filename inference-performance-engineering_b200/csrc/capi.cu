@@ -56,6 +56,7 @@ cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 namespace ipe {
 // Lets entry points defined in other files set the calling thread's ipe_last_error() message.
 int report_failure(int status, const char* message) { return fail(status, "%s", message); }
+int* device_error_word_ptr() { return device_error_word(); }
 }  // namespace ipe
 
 extern "C" {
@@ -318,7 +319,8 @@ int ipe_decode_attention(const void* q, const void* k_cache, const void* v_cache
     return fail(IPE_ERR_ARGUMENT, "ipe_decode_attention: workspace of %zu bytes needed",
                 ipe_decode_attention_workspace(batch, q_heads, capacity));
   return cuda_status(ipe::launch_decode_attention(q, k_cache, v_cache, out, batch, q_heads, kv_heads, capacity, length,
-                                                  state, static_cast<float*>(workspace), as_stream(stream)),
+                                                  state, static_cast<float*>(workspace), device_error_word(),
+                                                  as_stream(stream)),
                      "ipe_decode_attention");
 }
 
@@ -355,14 +357,6 @@ int ipe_prefill_attention(const void* q, const void* k_cache, const void* v_cach
     return fail(IPE_ERR_ARGUMENT, "ipe_prefill_attention: tokens %d outside 1..%d", tokens, capacity);
   if (!aligned16(q) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(out))
     return fail(IPE_ERR_ARGUMENT, "ipe_prefill_attention: q, caches and out must be 16-byte aligned (TMA)");
-  static const bool mma_sync = [] {  // measurement switch: the earlier mma.sync kernel
-    const char* v = std::getenv("IPE_PREFILL_ATTENTION_MMA");
-    return v && v[0] == '1';
-  }();
-  if (mma_sync)
-    return cuda_status(ipe::launch_prefill_attention(q, k_cache, v_cache, out, batch, q_heads, kv_heads, tokens,
-                                                     capacity, as_stream(stream)),
-                       "ipe_prefill_attention");
   return cuda_status(ipe::launch_prefill_attention_tc(q, k_cache, v_cache, out, batch, q_heads, kv_heads, tokens,
                                                       capacity, device_error_word(), as_stream(stream)),
                      "ipe_prefill_attention");

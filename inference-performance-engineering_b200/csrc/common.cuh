@@ -174,13 +174,14 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Bounded wait: returns false (and reports) if the phase did not complete within the limit.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+// Bounded wait: returns false (and reports) if the phase did not complete within limit_ns.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t start = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer_ns() - start > kWaitLimitNs) {
+    if ((i & 255u) == 0 && globaltimer_ns() - start > limit_ns) {
       report(err, kErrWaitTimeout);
       return false;
     }

@@ -83,7 +83,8 @@ extern "C" int ipe_decode_attention_static_scratch(const void* q, const void* k_
   float* scratch = scratch_on_current_device(&status);
   if (!scratch) return status;
   cudaError_t e = ipe::launch_decode_attention(q, k_cache, v_cache, out, batch, q_heads, kv_heads, capacity, length,
-                                               state, scratch, static_cast<cudaStream_t>(stream));
+                                               state, scratch, ipe::device_error_word_ptr(),
+                                               static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return ipe::report_failure(IPE_ERR_CUDA, cudaGetErrorString(e));
   return IPE_OK;
 }

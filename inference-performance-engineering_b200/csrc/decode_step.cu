@@ -60,6 +60,7 @@ struct StepArgs {
   int light_fences;         // grid barrier: acq_rel fence before the arrival, no fence after the acquire load
   int overlap_epilogue;     // warps 1-3 start the next unit while warp 0 runs this unit's epilogue
   float* cta_records;       // [grid][batch][IPE_PARTIAL_WORDS]: each CTA's merge of its LM-head records
+  uint64_t wait_ns;         // bound of every spin-wait
   // tensor parallelism (d.tp_world > 1): byte offsets in a communication region
   size_t recv_x;            // [2 slots][world][batch][hidden / 16][8 lines] parts of o_proj / down_proj
   size_t recv_rec;          // [world][grid][batch][3 lines] the CTAs' merged LM-head records
@@ -97,7 +98,7 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
       if ((i & 63u) == 63u) {
         const uint64_t now = globaltimer_ns();
         if (start == 0) start = now;
-        else if (now - start > kWaitLimitNs) {
+        else if (now - start > a.wait_ns) {
           report(a.err, kErrWaitTimeout);
           atomicExch(&a.grid_bar[1], 1u);
           *abort_smem = 1;
@@ -118,9 +119,12 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
 // --------------------------------------------------------------------- tensor parallelism
 // Communication region of a rank (ipe_decode_step_comm_bytes): the epoch counter at byte 128 (the
 // last exchange epoch of the previous step), then the receive buffers. Every value a peer sends is
-// a flagged line: 16 bytes {value, epoch, value, epoch} written by one 16-byte store, so a reader
-// that sees the current epoch in both flag words holds both values (the exchange needs no fence
-// and no barrier; each exchange has its own epoch, so a line from an earlier one never passes).
+// a flagged element: one naturally aligned 64-bit word {value (low 32 bits), epoch (high 32 bits)},
+// and a 16-byte line holds two of them. Lines are written and read as vectors of two 64-bit
+// elements; the memory model makes each 64-bit element a single-copy-atomic access (a vector is not
+// atomic as a whole), so a reader that sees the current epoch in an element holds that element's
+// value. The exchange needs no fence and no barrier; each exchange has its own epoch, so an element
+// from an earlier one never passes.
 constexpr size_t kTpCounter = 128;
 constexpr size_t kTpRecv = 256;
 constexpr size_t kTpLine = 16;
@@ -130,19 +134,19 @@ __device__ __forceinline__ unsigned char* tp_region(const ipe_decode_step_desc& 
   return reinterpret_cast<unsigned char*>(static_cast<const uint64_t*>(d.tp_peers)[r]);
 }
 
+// Two flagged elements {w0, epoch} and {w1, epoch}, each one 64-bit access.
 __device__ __forceinline__ void st_line(void* p, uint32_t w0, uint32_t w1, unsigned epoch) {
-  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(w0), "r"(epoch), "r"(w1),
-               "r"(epoch)
-               : "memory");
+  const uint64_t e0 = (static_cast<uint64_t>(epoch) << 32) | w0;
+  const uint64_t e1 = (static_cast<uint64_t>(epoch) << 32) | w1;
+  asm volatile("st.volatile.global.v2.b64 [%0], {%1, %2};" ::"l"(p), "l"(e0), "l"(e1) : "memory");
 }
 
+// The line's elements as {value 0, epoch 0, value 1, epoch 1}.
 __device__ __forceinline__ uint4 ld_line(const void* p) {
-  uint4 v;
-  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
+  uint64_t e0, e1;
+  asm volatile("ld.volatile.global.v2.b64 {%0, %1}, [%2];" : "=l"(e0), "=l"(e1) : "l"(p) : "memory");
+  return make_uint4(static_cast<uint32_t>(e0), static_cast<uint32_t>(e0 >> 32), static_cast<uint32_t>(e1),
+                    static_cast<uint32_t>(e1 >> 32));
 }
 
 __device__ __forceinline__ bool line_ready(const uint4& v, unsigned epoch) { return v.y == epoch && v.w == epoch; }
@@ -159,7 +163,7 @@ __device__ __noinline__ uint4 wait_line(const StepArgs& a, const void* p, unsign
       if (ld_acquire(&a.grid_bar[1])) return v;
       const uint64_t now = globaltimer_ns();
       if (start == 0) start = now;
-      else if (now - start > kWaitLimitNs) {
+      else if (now - start > a.wait_ns) {
         report(a.err, kErrWaitTimeout);
         atomicExch(&a.grid_bar[1], 1u);
         return v;
@@ -506,7 +510,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
             if (t >= ph.ku || !ok) continue;
             const bool two = pair && t + kConsumers < ph.ku;
             const int slot = w * S + sc[w].slot;
-            if (sc[w].fill > 0 && !mbar_wait(&empty[slot], (sc[w].fill - 1) & 1, a.err)) {
+            if (sc[w].fill > 0 && !mbar_wait(&empty[slot], (sc[w].fill - 1) & 1, a.err, a.wait_ns)) {
               ok = false;
               continue;
             }
@@ -609,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       if (res)
         for (int b = 0; b < B; ++b) bulk_copy(smem_addr(xres + b * H), res + b * H, res_bytes, &stage_bar);
     }
-    if (!mbar_wait(&stage_bar, stage_parity, a.err)) {
+    if (!mbar_wait(&stage_bar, stage_parity, a.err, a.wait_ns)) {
       atomicExch(&a.grid_bar[1], 1u);  // every CTA leaves at its next barrier
       *abort_smem = 1;
     }
@@ -738,7 +742,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
           const uint32_t base = smem_addr(ring + slot * kTileBytes);
           uint4 xv[4][NT];
           load_activations<NT>(xv, tt * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
-          if (!mbar_wait(&full[slot], mine.fill & 1, a.err)) {
+          if (!mbar_wait(&full[slot], mine.fill & 1, a.err, a.wait_ns)) {
             ok = false;
             break;
           }
@@ -1096,6 +1100,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   StepArgs a{};
   a.d = d;
   a.err = err;
+  a.wait_ns = d.wait_limit_ns > 0 ? static_cast<uint64_t>(d.wait_limit_ns) : kWaitLimitNs;
   a.max_splits = attn_max_splits(sm_count(), d.batch, d.kv_heads);
   unsigned char* ws = static_cast<unsigned char*>(d.workspace);
   a.grid_bar = reinterpret_cast<unsigned*>(ws);

@@ -57,11 +57,13 @@ void launch_sample(const float* partials, int parts, const float* logits, int ba
 void launch_sample_logits(const float* logits, int64_t rows, int vocab, float temperature, uint64_t seed,
                           int64_t* tokens, float* logprobs, int64_t stride, cudaStream_t stream);
 
-// Attention (attention_decode.cu, attention_prefill.cu).
+// Attention (attention_decode.cu, attention_prefill_tc.cu).
 int decode_attention_chunk();
 cudaError_t launch_decode_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                     int kv_heads, int capacity, int length, const int64_t* state, float* workspace,
-                                    cudaStream_t stream);
+                                    int* err, cudaStream_t stream);
+// The calling device's error word (the first device-side failure code since the last reset), or null.
+int* device_error_word_ptr();
 size_t fused_decode_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity);
 cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, const void* k_norm, const void* cos_t,
                                           const void* sin_t, const int64_t* state, int start, void* k_cache,
@@ -69,8 +71,6 @@ cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, c
                                           float eps, void* workspace, int* err, cudaStream_t stream);
 cudaError_t launch_prefill_attention_tc(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
                                         int kv_heads, int tokens, int capacity, int* err, cudaStream_t stream);
-cudaError_t launch_prefill_attention(const void* q, const void* k, const void* v, void* out, int batch, int q_heads,
-                                     int kv_heads, int tokens, int capacity, cudaStream_t stream);
 
 // Whole decode step (decode_step.cu).
 size_t decode_step_workspace_bytes(int batch, int q_heads, int kv_heads, int capacity);

@@ -94,7 +94,7 @@ class StepDesc(ctypes.Structure):
                 ("partials", c_void_p), ("workspace", c_void_p), ("workspace_bytes", c_size_t),
                 ("history_tokens", c_void_p), ("history_logprobs", c_void_p), ("history_stride", c_int64),
                 ("trace", c_void_p), ("tp_world", c_int), ("tp_rank", c_int), ("tp_peers", c_void_p),
-                ("x_alt", c_void_p), ("vocab_offset", c_int), ("vocab_total", c_int)]
+                ("x_alt", c_void_p), ("vocab_offset", c_int), ("vocab_total", c_int), ("wait_limit_ns", c_int64)]
 
 
 def trace_words(layers: int) -> int:

@@ -51,21 +51,36 @@ def sample(logits: torch.Tensor, temperature: float,
     """Tokens [B] and untempered log-probabilities [B] from fp32 logits [B, V] on the GPU.
 
     Temperature 0: argmax, lowest ID on ties. Otherwise Gumbel-max, argmax(l / T - log(-log U)),
-    with U from a counter-based generator keyed by a 64-bit seed drawn from `generator` (so the
+    with U from a counter-based generator keyed by a 64-bit seed taken from `generator` (so the
     same generator seed gives the same draws). No host sync (src/ipe/engine.py:28-41).
     """
     if temperature == 0:
         return ops.sample_logits(logits.contiguous(), 0.0, 0)
-    seed = torch.randint(0, 2**62, (1,), generator=generator, device=generator.device if generator else "cpu")
-    return ops.sample_logits(logits.contiguous(), float(temperature), int(seed.item()))
+    return ops.sample_logits(logits.contiguous(), float(temperature), _generator_seed(generator))
 
 
-def _step_seed(seed: int, step: int) -> int:
-    """A 64-bit seed per generation step for the fp32 path's sampler (splitmix64 finaliser)."""
-    z = (seed + 0x9E3779B97F4A7C15 * (step + 1)) & (2**64 - 1)
+def _mix64(z: int) -> int:
+    """splitmix64's finaliser: a 64-bit bijection that spreads every input bit."""
+    z &= 2**64 - 1
     z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & (2**64 - 1)
     z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & (2**64 - 1)
     return z ^ (z >> 31)
+
+
+def _generator_seed(generator: torch.Generator | None) -> int:
+    """A 64-bit seed from `generator`, advancing it, without reading device memory: a CPU
+    generator draws on the host; a CUDA generator's seed and Philox offset are host-side state,
+    so the seed mixes the two and the offset moves on by one draw."""
+    if generator is None or generator.device.type == "cpu":
+        return int(torch.randint(0, 2**62, (1,), generator=generator).item())
+    offset = generator.get_offset()
+    generator.set_offset(offset + 4)
+    return _mix64(generator.initial_seed() ^ _mix64(0x9E3779B97F4A7C15 * (offset // 4 + 1)))
+
+
+def _step_seed(seed: int, step: int) -> int:
+    """A 64-bit seed per generation step for the fp32 path's sampler."""
+    return _mix64(seed + 0x9E3779B97F4A7C15 * (step + 1))
 
 
 def _float_bits(value: float) -> int:

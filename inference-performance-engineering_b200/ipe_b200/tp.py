@@ -171,7 +171,11 @@ class TensorParallelEngine:
     same order). The weights in `loaded` must be bf16 on this rank's GPU; only this rank's shard is
     kept (plus the embedding and the norms, replicated)."""
 
-    def __init__(self, loaded, *, batch: int, capacity: int, group=None, allreduce: str = "fused"):
+    def __init__(self, loaded, *, batch: int, capacity: int, group=None, allreduce: str = "fused",
+                 wait_limit_s: float = 2.0):
+        """wait_limit_s bounds every wait of the one-kernel step on the device, a peer's parts among
+        them: a peer that stops answering makes this rank's step give up after that long, set
+        device error 3 and commit nothing; `generate` then raises."""
         c, w = loaded.config, loaded.weights
         check_supported(c)
         if w.embed_tokens.dtype != torch.bfloat16 or w.embed_tokens.device.type != "cuda":
@@ -180,6 +184,10 @@ class TensorParallelEngine:
             raise ValueError(f"batch {batch!r}: expected 1..16")
         if not (type(capacity) is int and 1 <= capacity <= c.max_position_embeddings):
             raise ValueError(f"capacity {capacity!r}")
+        if not (isinstance(wait_limit_s, (int, float)) and 0 < wait_limit_s <= 60):
+            raise ValueError(f"wait_limit_s {wait_limit_s!r}: expected a number of seconds in (0, 60]")
+        self.wait_limit_ns = int(wait_limit_s * 1e9)
+        self.failed: str | None = None  # set once a step failed on the device; the engine is then spent
         self.group = group
         self.world = dist.get_world_size(group)
         self.plan = p = shard_plan(c, dist.get_rank(group), self.world)
@@ -292,6 +300,7 @@ class TensorParallelEngine:
             d.history_stride = self.history_tokens.shape[1]
         d.tp_world, d.tp_rank, d.tp_peers = self.world, p.rank, self._peer.table.data_ptr()
         d.x_alt, d.vocab_offset, d.vocab_total = self.x_alt.data_ptr(), p.vocab_offset, c.vocab_size
+        d.wait_limit_ns = self.wait_limit_ns
         self._descs[key] = d
         return d
 
@@ -479,6 +488,8 @@ class TensorParallelEngine:
             raise ValueError("decode: no batch; call prefill first")
         if self.length == self.capacity:
             raise ValueError(f"decode: all {self.capacity} positions are committed")
+        if self.failed:
+            raise RuntimeError(f"tensor-parallel engine: an earlier step failed ({self.failed}); build a new engine")
         if not isinstance(tokens, torch.Tensor) or tokens.shape != (self.batch,):
             raise ValueError(f"tokens: expected integer IDs of shape [{self.batch}]")
         stream = torch.cuda.current_stream().cuda_stream
@@ -515,6 +526,9 @@ class TensorParallelEngine:
         lib, stream, st = nat.load(), torch.cuda.current_stream().cuda_stream, self.state.data_ptr()
         if batch > self.max_batch:
             raise ValueError(f"token_ids: batch {batch} exceeds the {self.max_batch} allocated rows")
+        if self.failed:
+            raise RuntimeError(f"tensor-parallel engine: an earlier step failed ({self.failed}); build a new engine")
+        nat.device_error(reset=True)  # the check below sees only this call's failures
         nat.check(lib.ipe_state_set(st, nat.STATE_STEP, 0, stream), "ipe_state_set")
         nat.check(lib.ipe_state_set(st, nat.STATE_SEED, int(seed) & (2**63 - 1), stream), "ipe_state_set")
         bits = struct.unpack("<i", struct.pack("<f", float(temperature)))[0]
@@ -527,6 +541,16 @@ class TensorParallelEngine:
                 self._step_graph()
         finally:
             nat.check(lib.ipe_state_set(st, nat.STATE_TEMPERATURE, 0, stream), "ipe_state_set")
+        tokens = self.history_tokens[:batch, :max_new_tokens].cpu()
+        logprobs = self.history_logprobs[:batch, :max_new_tokens].cpu()
+        code = nat.device_error(reset=True)
+        if code:
+            # a step whose wait ran out (a peer that stopped answering) committed nothing: the
+            # device position is the committed prefix, and the exchange epochs are spent
+            self.length = int(self.state[nat.STATE_POS].item())
+            self.failed = f"device error {code}"
+            raise RuntimeError(f"tensor-parallel generate: a decode step failed on the device (error {code}: "
+                               f"{'a wait ran out' if code == 3 else 'see ipe_device_error'}); "
+                               f"{self.length} positions committed")
         self.length = length + max_new_tokens - 1
-        return (self.history_tokens[:batch, :max_new_tokens].cpu(),
-                self.history_logprobs[:batch, :max_new_tokens].cpu())
+        return tokens, logprobs

@@ -2,7 +2,7 @@
 
 Run in a container that has the reference checkout (read-only is fine):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path of the reference checkout>
 
 It imports the reference package `ipe` from `<reference>/src` (torch CPU), builds seeded synthetic
 models with `ipe_b200.synthetic.random_model`, wraps the same tensors in the reference's own
@@ -65,7 +65,7 @@ def to_reference(ipe_weights, ipe_config, loaded):
 
 def main() -> None:
     parser = argparse.ArgumentParser()
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True, help="path of the reference checkout (its src/ holds ipe)")
     parser.add_argument("--only", nargs="*")
     args = parser.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "src"))

@@ -245,6 +245,23 @@ def test_decode_steps_never_synchronize_or_grow_the_allocator(models):
     assert torch.cuda.memory_reserved() == reserved
 
 
+def test_tempered_sample_with_a_cuda_generator_never_synchronizes():
+    logits = torch.randn((3, 4096), generator=torch.Generator().manual_seed(2)).cuda()
+    first = torch.Generator(device="cuda").manual_seed(11)
+    again = torch.Generator(device="cuda").manual_seed(11)
+    torch.cuda.synchronize()
+    torch.cuda.set_sync_debug_mode("error")
+    try:
+        a1, a2 = sample(logits, 0.8, first)[0], sample(logits, 0.8, first)[0]
+        b1 = sample(logits, 0.8, again)[0]
+    finally:
+        torch.cuda.set_sync_debug_mode(0)
+    # the same generator seed gives the same draws; a generator moves on after each draw
+    assert torch.equal(a1, b1)
+    draws = torch.stack([sample(logits, 0.8, first)[0] for _ in range(6)] + [a1, a2])
+    assert len({tuple(r.tolist()) for r in draws}) > 1
+
+
 @pytest.mark.parametrize(("name", "batch", "length", "prompt"), [
     ("small", 2, 20, 6),
     ("qwen3-1.7b-2layer", 1, 700, 694),   # one row: 11 attention splits merged, half-tile o/down units
