@@ -133,67 +133,86 @@ def read_header(path: str | PathLike[str], file: str | None = None) -> dict[str,
     return tensors
 
 
-def inspect_checkpoint(directory: str | PathLike[str]) -> dict[str, TensorInfo]:
-    """Every stored tensor's dtype, shape, file and byte range, from headers alone."""
-    root = Path(directory)
-    top_level = set(os.listdir(root))
-    has_single, has_index = SINGLE_FILE in top_level, INDEX_FILE in top_level
-    if has_single == has_index:
+def _shard_files(root: Path, entries: set[str]) -> tuple[list[str], dict[str, str] | None]:
+    """The safetensors files a checkpoint directory must hold, and its index's name -> file map
+    (None for a single-file checkpoint). A directory holds exactly one of model.safetensors or an
+    index, and no safetensors file the layout does not name."""
+    layouts = [name for name in (SINGLE_FILE, INDEX_FILE) if name in entries]
+    if len(layouts) != 1:
         raise CheckpointError(f"{root}: expected exactly one of {SINGLE_FILE} or {INDEX_FILE}")
-    if has_index:
+    weight_map = None
+    files = [SINGLE_FILE]
+    if layouts[0] == INDEX_FILE:
         try:
-            weight_map = json.loads((root / INDEX_FILE).read_text(encoding="utf-8"))["weight_map"]
-            files = sorted(set(weight_map.values()))
+            weight_map = dict(json.loads((root / INDEX_FILE).read_text(encoding="utf-8"))["weight_map"])
+            files = sorted({str(f) for f in weight_map.values()})
         except (ValueError, KeyError, TypeError, AttributeError) as error:
             raise CheckpointError(f"{INDEX_FILE}: malformed ({error!r})") from error
-    else:
-        files = [SINGLE_FILE]
-    found = sorted(name for name in top_level if name.endswith(".safetensors"))
-    if found != files:
-        raise CheckpointError(f"{root}: safetensors files {found}, expected {files}")
+    present = sorted(e for e in entries if e.endswith(".safetensors"))
+    if present != files:
+        raise CheckpointError(f"{root}: safetensors files {present}, expected {files}")
+    return files, weight_map
+
+
+def inspect_checkpoint(directory: str | PathLike[str]) -> dict[str, TensorInfo]:
+    """Every stored tensor's dtype, shape, file and byte range, from headers alone, sorted by name
+    (the rules of src/ipe/checkpoint.py:131-164: one layout, no stray files, no tensor stored
+    twice, an index that maps exactly the stored names)."""
+    root = Path(directory)
+    files, weight_map = _shard_files(root, set(os.listdir(root)))
     inventory: dict[str, TensorInfo] = {}
     for file in files:
-        for name, info in read_header(root / file, file).items():
-            if name in inventory:
-                raise CheckpointError(f"{name}: stored in both {inventory[name].file} and {file}")
-            inventory[name] = info
-    if has_index and set(weight_map) != set(inventory):
-        unmatched = sorted(set(weight_map) ^ set(inventory))
-        raise CheckpointError(f"{INDEX_FILE}: names mapped or stored, but not both: {unmatched}")
-    return dict(sorted(inventory.items()))
+        header = read_header(root / file, file)
+        for name in header.keys() & inventory.keys():
+            raise CheckpointError(f"{name}: stored in both {inventory[name].file} and {file}")
+        inventory.update(header)
+    if weight_map is not None:
+        unmatched = sorted(weight_map.keys() ^ inventory.keys())
+        if unmatched:
+            raise CheckpointError(f"{INDEX_FILE}: names mapped or stored, but not both: {unmatched}")
+    return {name: inventory[name] for name in sorted(inventory)}
 
 
 # ------------------------------------------------------------------------------------ mapping
 
 def layer_shapes(config: Qwen3Config) -> dict[str, tuple[int, ...]]:
-    h, i = config.hidden_size, config.intermediate_size
-    q, kv = config.num_attention_heads * config.head_dim, config.num_key_value_heads * config.head_dim
-    return {"input_layernorm": (h,), "q_proj": (q, h), "k_proj": (kv, h), "v_proj": (kv, h),
-            "q_norm": (config.head_dim,), "k_norm": (config.head_dim,), "o_proj": (h, q),
-            "post_attention_layernorm": (h,), "gate_proj": (i, h), "up_proj": (i, h), "down_proj": (h, i)}
+    """The [out, in] (or [n]) shape of each per-layer engine field."""
+    c = config
+    q_out, kv_out = c.num_attention_heads * c.head_dim, c.num_key_value_heads * c.head_dim
+    vector, head = (c.hidden_size,), (c.head_dim,)
+    into_hidden, from_hidden = (c.hidden_size, c.intermediate_size), (c.intermediate_size, c.hidden_size)
+    table = dict(input_layernorm=vector, post_attention_layernorm=vector, q_norm=head, k_norm=head,
+                 q_proj=(q_out, c.hidden_size), k_proj=(kv_out, c.hidden_size), v_proj=(kv_out, c.hidden_size),
+                 o_proj=(c.hidden_size, q_out), gate_proj=from_hidden, up_proj=from_hidden, down_proj=into_hidden)
+    return {field: table[field] for field in LAYER_TENSORS}
 
 
 def expected_tensors(config: Qwen3Config) -> dict[str, tuple[int, ...]]:
     """Every tensor the engine consumes, with its shape (the optional stored LM head excluded)."""
-    expected = {EMBED_TOKENS: (config.vocab_size, config.hidden_size)}
-    shapes = layer_shapes(config)
-    for layer in range(config.num_hidden_layers):
-        for field, suffix in LAYER_TENSORS.items():
-            expected[f"model.layers.{layer}.{suffix}"] = shapes[field]
-    expected[FINAL_NORM] = (config.hidden_size,)
-    return expected
+    per_layer = layer_shapes(config)
+    names = [(EMBED_TOKENS, (config.vocab_size, config.hidden_size))]
+    names += [(f"model.layers.{i}.{suffix}", per_layer[field]) for i in range(config.num_hidden_layers)
+              for field, suffix in LAYER_TENSORS.items()]
+    names.append((FINAL_NORM, (config.hidden_size,)))
+    return dict(names)
 
 
 def check_mapping(inventory: dict[str, TensorInfo], config: Qwen3Config) -> None:
-    """Every expected tensor stored as BF16 with its shape, nothing else; an optional LM head."""
-    allowed = expected_tensors(config)
-    missing = sorted(set(allowed) - set(inventory))
-    allowed[LM_HEAD] = (config.vocab_size, config.hidden_size)
-    stored = sorted(inventory.items())
-    unexpected = [f"{name} in {info.file}" for name, info in stored if name not in allowed]
-    mismatched = [f"{name} in {info.file}: {info.dtype} {list(info.shape)}, expected {STORED_DTYPE} "
-                  f"{list(allowed[name])}" for name, info in stored
-                  if name in allowed and (info.dtype != STORED_DTYPE or info.shape != allowed[name])]
+    """Every expected tensor stored as BF16 with its shape and nothing else, plus an optional LM
+    head of the embedding's shape (src/ipe/checkpoint.py:184-217); one CheckpointError lists every
+    problem."""
+    required = expected_tensors(config)
+    optional = {LM_HEAD: (config.vocab_size, config.hidden_size)}
+    missing = sorted(name for name in required if name not in inventory)
+    unexpected, mismatched = [], []
+    for name in sorted(inventory):
+        info = inventory[name]
+        shape = required.get(name, optional.get(name))
+        if shape is None:
+            unexpected.append(f"{name} in {info.file}")
+        elif (info.dtype, tuple(info.shape)) != (STORED_DTYPE, shape):
+            mismatched.append(f"{name} in {info.file}: {info.dtype} {list(info.shape)}, expected {STORED_DTYPE} "
+                              f"{list(shape)}")
     if missing or unexpected or mismatched:
         raise CheckpointError("checkpoint does not match the configuration: "
                               f"{len(missing)} missing {missing}, {len(unexpected)} unexpected {unexpected}, "

@@ -25,16 +25,22 @@ import torch
 
 from ipe_b200 import _native as nat
 from ipe_b200 import fp32 as _fp32
+from ipe_b200 import layer as _layer
 from ipe_b200 import model as _model
 from ipe_b200 import ops
 from ipe_b200.forward import INTEGER_DTYPES, check_backend, check_dtype, check_token_ids
 
-# The per-layer launch sequences. `_step` calls these module globals for every layer, so a test
-# can replace one to inject a failure; the decode CUDA graph is only used while they are the
-# built-in functions.
-prefill_layer = _model.prefill_layer
-decoder_layer = _model.decode_layer
-_BUILTIN_DECODE = _model.decode_layer
+# One decoder layer, with the reference's signature (x, layer, rope, config, *, backend, cache=None,
+# start=0) (src/ipe/forward.py:86-115). While this module global is the built-in function, steps
+# run the engine's fused paths (the one-kernel decode step from a CUDA graph, the fused prefill
+# chain). A caller that replaces it (to wrap, count or fail a layer, as the reference's tests do,
+# src/ipe/engine.py:107-109) gets it called for every layer of every step, as the reference does.
+decoder_layer = _layer.decoder_layer
+_BUILTIN_DECODE = _layer.decoder_layer
+
+
+def _hooked() -> bool:
+    return decoder_layer is not _BUILTIN_DECODE
 
 
 @dataclass(frozen=True, slots=True)
@@ -173,7 +179,7 @@ class Engine:
         _, length = check_token_ids(self.loaded.config, token_ids, self.capacity)
         if length + max_new_tokens - 1 > self.capacity:
             raise ValueError(f"prompt length {length} + max_new_tokens {max_new_tokens} - 1 exceeds capacity {self.capacity}")
-        run = self._generate_f32 if self._f32 is not None else self._generate_on_device
+        run = self._generate_stepwise if self._f32 is not None or _hooked() else self._generate_on_device
         tokens, logprobs, lengths, produced = run(token_ids, max_new_tokens, float(temperature), int(seed),
                                                   tuple(stop_ids))
         return Generation(tokens[:, :produced].cpu(), logprobs[:, :produced].cpu(), lengths.cpu())
@@ -220,10 +226,11 @@ class Engine:
             nat.check(lib.ipe_state_set(state, nat.STATE_TEMPERATURE, 0, stream), "ipe_state_set")
         return tokens[:, :max_new_tokens].clone(), logprobs[:, :max_new_tokens].clone(), lengths, produced
 
-    def _generate_f32(self, token_ids, max_new_tokens: int, temperature: float, seed: int,
-                      stop_ids: tuple[int, ...] = ()):
-        """The fp32 generation loop: prefill, then per token the library sampler on the step's fp32
-        logits (Gumbel draws keyed by a per-step seed) and a decode step on the sampled IDs."""
+    def _generate_stepwise(self, token_ids, max_new_tokens: int, temperature: float, seed: int,
+                           stop_ids: tuple[int, ...] = ()):
+        """The generation loop of the fp32 path and of a replaced layer hook: prefill, then per
+        token the library sampler on the step's fp32 logits (Gumbel draws keyed by a per-step seed)
+        and a decode step on the sampled IDs (src/ipe/engine.py:137-147)."""
         logits = self.prefill(token_ids)
         device, batch = self._f32.device, self.batch
         tokens = torch.empty((batch, max_new_tokens), dtype=torch.int64, device=device)
@@ -266,6 +273,8 @@ class Engine:
     def _step(self, token_ids: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor], start: int) -> torch.Tensor:
         """Run all layers for token_ids [B, T] at positions start..start+T-1 and the LM head on the
         last position; fp32 logits [B, V] in the engine's logits buffer (src/ipe/engine.py:103-111)."""
+        if _hooked():
+            return self._step_hooked(token_ids, rope, start)
         if self._f32 is not None:
             return self._step_f32(token_ids, start)
         if start == 0:
@@ -276,6 +285,38 @@ class Engine:
         self._buf.tokens[:b].copy_(token_ids[:, 0], non_blocking=True)
         self._run_decode(start, batch=b)
         return self._buf.logits[:b]
+
+    def _step_hooked(self, token_ids: torch.Tensor, rope: tuple[torch.Tensor, torch.Tensor], start: int) -> torch.Tensor:
+        """The reference's step structure (src/ipe/engine.py:103-111) around a replaced layer hook:
+        embedding, the module global `decoder_layer` for every layer with the layer's cache rows,
+        then the final norm of each row's last position and the tied LM head, on the CUDA kernels."""
+        c, w = self.loaded.config, self.loaded.weights
+        batch, length = token_ids.shape
+        if start > 0 and length != 1:
+            raise ValueError("decoder_layer: a step after position 0 takes one token; chunked prefill is not supported")
+        device = self._k.device
+        stream = torch.cuda.current_stream().cuda_stream
+        lib = nat.load()
+        ids = token_ids.to(device=device, dtype=torch.int64).reshape(-1).contiguous()
+        x = torch.empty((batch * length, c.hidden_size), dtype=self.dtype, device=device)
+        table = self._f32.embed if self._f32 is not None else self._model.embed
+        embed = lib.ipe_embed_f32 if self._f32 is not None else lib.ipe_embed
+        nat.check(embed(ids.data_ptr(), ids.numel(), table.data_ptr(), c.vocab_size, c.hidden_size, x.data_ptr(),
+                        stream), "ipe_embed")
+        x = x.view(batch, length, c.hidden_size)
+        for index, layer in enumerate(w.layers):
+            cache = (self._k[index, :batch], self._v[index, :batch])
+            x = decoder_layer(x, layer, rope, c, backend=self.backend, cache=cache, start=start)
+        last = x[:, -1].contiguous()
+        if self._f32 is not None:
+            hidden = _fp32.final_norm(self._f32, last, torch.empty_like(last), stream)
+            logits = torch.empty((batch, c.vocab_size), dtype=torch.float32, device=device)
+            return _fp32.lm_logits(self._f32, hidden, logits, stream)
+        m, buf = self._model, self._buf
+        nat.check(lib.ipe_lm_head(last.data_ptr(), c.hidden_size, m.final_norm.data_ptr(), m.t_lm_head.data_ptr(),
+                                  buf.logits.data_ptr(), buf.partials.data_ptr(), batch, c.hidden_size, c.vocab_size,
+                                  c.rms_norm_eps, 0.0, 0, buf.state.data_ptr(), stream), "ipe_lm_head")
+        return buf.logits[:batch]
 
     def _step_f32(self, token_ids: torch.Tensor, start: int) -> torch.Tensor:
         """The fp32 path of _step: token_ids [B, T] at positions start.., logits of each row's last
@@ -308,8 +349,8 @@ class Engine:
                                 buf.x.data_ptr(), stream), "ipe_embed")
         cos, sin = rope
         for index in range(c.num_hidden_layers):
-            prefill_layer(m, index, buf, self._k[index], self._v[index], batch, length, self.capacity, cos, sin,
-                          stream)
+            _model.prefill_layer(m, index, buf, self._k[index], self._v[index], batch, length, self.capacity, cos, sin,
+                                 stream)
         last = buf.x.data_ptr() + (length - 1) * c.hidden_size * 2
         nat.check(lib.ipe_lm_head(last, length * c.hidden_size, m.final_norm.data_ptr(), m.t_lm_head.data_ptr(),
                                   self._buf.logits.data_ptr(), self._buf.partials.data_ptr(), batch, c.hidden_size,
@@ -318,18 +359,6 @@ class Engine:
         nat.check(lib.ipe_state_set(self._buf.state.data_ptr(), nat.STATE_POS, length, stream), "ipe_state_set")
         self._device_pos = length
         return self._buf.logits[:batch]
-
-    def _launch_decode(self, batch: int, stream: int) -> None:
-        c, m, buf, lib = self.loaded.config, self._model, self._buf, nat.load()
-        nat.check(lib.ipe_embed(buf.tokens.data_ptr(), batch, m.embed.data_ptr(), c.vocab_size, c.hidden_size,
-                                buf.x.data_ptr(), stream), "ipe_embed")
-        for index in range(c.num_hidden_layers):
-            decoder_layer(m, index, buf, self._k[index], self._v[index], batch, self.capacity, self._cos, self._sin,
-                          stream)
-        nat.check(lib.ipe_lm_head(buf.x.data_ptr(), c.hidden_size, m.final_norm.data_ptr(), m.t_lm_head.data_ptr(),
-                                  buf.logits.data_ptr(), buf.partials.data_ptr(), batch, c.hidden_size, c.vocab_size,
-                                  c.rms_norm_eps, 0.0, 0, buf.state.data_ptr(), stream), "ipe_lm_head")
-        nat.check(lib.ipe_state_add(buf.state.data_ptr(), nat.STATE_POS, 1, stream), "ipe_state_add")
 
     def _launch_step(self, batch: int, sample: bool, stream: int) -> None:
         """The whole decode step as one kernel (ipe_decode_step)."""
@@ -349,12 +378,7 @@ class Engine:
         if self._device_pos != start:
             nat.check(nat.load().ipe_state_set(self._buf.state.data_ptr(), nat.STATE_POS, start, stream),
                       "ipe_state_set")
-        if decoder_layer is not _BUILTIN_DECODE:
-            # a replaced per-layer hook runs the per-operator kernels eagerly, layer by layer
-            if sample:
-                raise RuntimeError("sampling decode steps need the built-in decode path")
-            self._launch_decode(batch, stream)
-        elif (batch, sample) not in self._warm:
+        if (batch, sample) not in self._warm:
             self._launch_step(batch, sample, stream)
             self._warm.add((batch, sample))
         else:

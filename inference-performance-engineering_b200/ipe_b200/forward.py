@@ -5,7 +5,8 @@ Drop-in for the reference's `ipe.forward` (src/ipe/forward.py):
 - `forward_full(loaded, token_ids, *, dtype, logit_positions=None, backend="math")`: fp32 logits
   [B, n, V] (bf16 logits widened), computed by the prefill kernels with a cache sized to the
   prompt (`:155-170`);
-- `final_hidden` / `lm_logits`: the final-normed states and the tied LM head (`:133-152`).
+- `final_hidden` / `lm_logits`: the final-normed states and the tied LM head (`:133-152`);
+- `decoder_layer`: one layer with the reference's signature (`:86-115`, ipe_b200.layer).
 
 The CUDA path computes in bf16 (weight-streaming and tcgen05 kernels) or in fp32 (the
 reference-precision kernels of ipe_b200.fp32, for the plumbing configuration). fp64 (the
@@ -20,6 +21,7 @@ from collections.abc import Sequence
 import torch
 
 from ipe_b200.config import check_supported
+from ipe_b200.layer import decoder_layer  # noqa: F401  (src/ipe/forward.py:86-115, the engine's per-layer hook)
 from ipe_b200.model import PackedModel, PrefillBuffers, packed_model, run_prefill_layers
 from ipe_b200 import fp32 as _fp32
 from ipe_b200 import ops
@@ -48,22 +50,30 @@ def check_dtype(loaded, dtype: torch.dtype, allowed: Sequence[torch.dtype]) -> N
     check_supported(loaded.config)
 
 
+def _within(values: torch.Tensor, upper: int) -> bool:
+    """Whether every integer in `values` lies in [0, upper), compared in int64 (a bound compared in
+    a narrower dtype would wrap). Syncs for GPU tensors."""
+    wide = values.to(torch.int64)
+    return bool(wide.min() >= 0) and bool(wide.max() < upper)
+
+
 def check_token_ids(config, token_ids: object, capacity: int) -> tuple[int, int]:
     """Integer IDs [B, T] in the vocabulary, 1 <= T <= capacity; (B, T). Syncs for GPU IDs
-    (src/ipe/forward.py:46-63)."""
+    (the admission and messages of src/ipe/forward.py:46-63)."""
     if not isinstance(token_ids, torch.Tensor):
         raise ValueError(f"token_ids: expected a tensor, got {type(token_ids).__name__}")
-    if token_ids.dtype not in INTEGER_DTYPES:
-        raise ValueError(f"token_ids: expected one of {list(INTEGER_DTYPES)}, got {token_ids.dtype}")
-    if token_ids.dim() != 2 or token_ids.shape[0] < 1:
-        raise ValueError(f"token_ids: expected shape [B, T] with B >= 1, got {list(token_ids.shape)}")
-    batch, length = token_ids.shape
-    if not 1 <= length <= capacity:
-        raise ValueError(f"token_ids: length {length} is outside 1 to {capacity}")
-    ids = token_ids.to(torch.int64)
-    if ids.min() < 0 or ids.max() >= config.vocab_size:
+    shape = list(token_ids.shape)
+    checks = (
+        (token_ids.dtype in INTEGER_DTYPES, lambda: f"expected one of {list(INTEGER_DTYPES)}, got {token_ids.dtype}"),
+        (len(shape) == 2 and shape[0] >= 1, lambda: f"expected shape [B, T] with B >= 1, got {shape}"),
+        (len(shape) == 2 and 1 <= shape[-1] <= capacity, lambda: f"length {shape[-1]} is outside 1 to {capacity}"),
+    )
+    for ok, message in checks:
+        if not ok:
+            raise ValueError(f"token_ids: {message()}")
+    if not _within(token_ids, config.vocab_size):
         raise ValueError(f"token_ids: IDs must lie in [0, {config.vocab_size})")
-    return batch, length
+    return shape[0], shape[1]
 
 
 def check_backend(backend: object) -> None:
@@ -72,6 +82,7 @@ def check_backend(backend: object) -> None:
 
 
 def _check_logit_positions(logit_positions: object, length: int) -> torch.Tensor:
+    """The requested positions as int64 [n], n >= 1, each in [0, length) (src/ipe/forward.py:71-83)."""
     try:
         rows = torch.as_tensor(logit_positions)
     except (TypeError, ValueError, RuntimeError) as error:
@@ -80,10 +91,9 @@ def _check_logit_positions(logit_positions: object, length: int) -> torch.Tensor
         raise ValueError(f"logit_positions: expected integers, got {rows.dtype}")
     if rows.dim() != 1 or rows.numel() == 0:
         raise ValueError("logit_positions: expected a non-empty 1-D sequence")
-    rows = rows.to(torch.int64)
-    if rows.min() < 0 or rows.max() >= length:
+    if not _within(rows, length):
         raise ValueError(f"logit_positions: positions must lie in [0, {length})")
-    return rows
+    return rows.to(torch.int64)
 
 
 def _uncached_hidden(model: PackedModel, token_ids: torch.Tensor) -> torch.Tensor:

@@ -15,6 +15,7 @@ from __future__ import annotations
 import torch
 
 from ipe_b200 import _native as nat
+from ipe_b200 import layer as layer_hook
 from ipe_b200.config import check_supported
 
 F32 = 1  # ipe_rmsnorm dtype code
@@ -56,6 +57,7 @@ class Fp32Model:
             self.layers = [Fp32Layer(layer, c) for layer in w.layers]
         self.q_rows = c.num_attention_heads * c.head_dim
         self.qkv_rows = self.q_rows + 2 * c.num_key_value_heads * c.head_dim
+        layer_hook.register(self, torch.float32)
         self._decode: tuple[torch.Tensor, torch.Tensor] | None = None
         self._prefill: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
 
@@ -109,38 +111,46 @@ class Fp32Buffers:
         self.logits = torch.empty((batch, c.vocab_size), dtype=f, device=dev)
 
 
+def layer_ops(c, layer: Fp32Layer, q_rows: int, qkv_rows: int, x: torch.Tensor, h: torch.Tensor, qkv: torch.Tensor,
+              q: torch.Tensor, attn: torch.Tensor, act: torch.Tensor, k_layer: torch.Tensor, v_layer: torch.Tensor,
+              batch: int, tokens: int, start: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor,
+              stream: int) -> None:
+    """One decoder layer (src/ipe/forward.py:86-115) for batch rows of `tokens` tokens at positions
+    start.., x [batch*tokens, H] updated in place; cos / sin tables indexed by position."""
+    lib = nat.load()
+    rows, hd, i = batch * tokens, c.hidden_size, c.intermediate_size
+    hq, hkv, eps = c.num_attention_heads, c.num_key_value_heads, c.rms_norm_eps
+    xp, hp = x.data_ptr(), h.data_ptr()
+    nat.check(lib.ipe_rmsnorm(xp, layer.in_norm.data_ptr(), hp, rows, hd, eps, F32, stream), "ipe_rmsnorm")
+    nat.check(lib.ipe_gemm_f32(hp, layer.w_qkv.data_ptr(), qkv.data_ptr(), rows, qkv_rows, hd, nat.EPI_STORE, None,
+                               stream), "ipe_gemm_f32 qkv")
+    nat.check(lib.ipe_qk_norm_rope_append_f32(qkv.data_ptr(), batch, tokens, hq, hkv, layer.q_norm.data_ptr(),
+                                              layer.k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(), start,
+                                              q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), capacity, eps,
+                                              stream), "ipe_qk_norm_rope_append_f32")
+    nat.check(lib.ipe_attention_f32(q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), attn.data_ptr(), batch, hq,
+                                    hkv, tokens, capacity, start, stream), "ipe_attention_f32")
+    nat.check(lib.ipe_gemm_f32(attn.data_ptr(), layer.w_o.data_ptr(), xp, rows, hd, q_rows, nat.EPI_RESIDUAL, xp,
+                               stream), "ipe_gemm_f32 o_proj")
+    nat.check(lib.ipe_rmsnorm(xp, layer.post_norm.data_ptr(), hp, rows, hd, eps, F32, stream), "ipe_rmsnorm")
+    nat.check(lib.ipe_gemm_f32(hp, layer.w_gate_up.data_ptr(), act.data_ptr(), rows, 2 * i, hd, nat.EPI_SILU_MUL,
+                               None, stream), "ipe_gemm_f32 gate_up")
+    nat.check(lib.ipe_gemm_f32(act.data_ptr(), layer.w_down.data_ptr(), xp, rows, hd, i, nat.EPI_RESIDUAL, xp, stream),
+              "ipe_gemm_f32 down_proj")
+
+
 def run_layers(model: Fp32Model, buf: Fp32Buffers, k: torch.Tensor, v: torch.Tensor, start: int, capacity: int,
                cos: torch.Tensor, sin: torch.Tensor, stream: int) -> None:
-    """Embedding of buf.ids and every decoder layer (src/ipe/forward.py:86-115) for buf.batch rows of
-    buf.tokens tokens at positions start.. ; the residual stream ends in buf.x. k / v: the fp32
-    caches [layers, batch rows, KV heads, capacity, 128]."""
+    """Embedding of buf.ids and every decoder layer for buf.batch rows of buf.tokens tokens at
+    positions start.. ; the residual stream ends in buf.x. k / v: the fp32 caches [layers, batch
+    rows, KV heads, capacity, 128]."""
     c, lib = model.config, nat.load()
-    batch, tokens = buf.batch, buf.tokens
-    rows, h, i = batch * tokens, c.hidden_size, c.intermediate_size
-    hq, hkv, eps = c.num_attention_heads, c.num_key_value_heads, c.rms_norm_eps
-    nat.check(lib.ipe_embed_f32(buf.ids.data_ptr(), rows, model.embed.data_ptr(), c.vocab_size, h, buf.x.data_ptr(),
-                                stream), "ipe_embed_f32")
-    x = buf.x.data_ptr()
+    rows = buf.batch * buf.tokens
+    nat.check(lib.ipe_embed_f32(buf.ids.data_ptr(), rows, model.embed.data_ptr(), c.vocab_size, c.hidden_size,
+                                buf.x.data_ptr(), stream), "ipe_embed_f32")
     for index, layer in enumerate(model.layers):
-        nat.check(lib.ipe_rmsnorm(x, layer.in_norm.data_ptr(), buf.h.data_ptr(), rows, h, eps, F32, stream),
-                  "ipe_rmsnorm")
-        nat.check(lib.ipe_gemm_f32(buf.h.data_ptr(), layer.w_qkv.data_ptr(), buf.qkv.data_ptr(), rows, model.qkv_rows,
-                                   h, nat.EPI_STORE, None, stream), "ipe_gemm_f32 qkv")
-        nat.check(lib.ipe_qk_norm_rope_append_f32(buf.qkv.data_ptr(), batch, tokens, hq, hkv, layer.q_norm.data_ptr(),
-                                                  layer.k_norm.data_ptr(), cos.data_ptr(), sin.data_ptr(), start,
-                                                  buf.q.data_ptr(), k[index].data_ptr(), v[index].data_ptr(), capacity,
-                                                  eps, stream), "ipe_qk_norm_rope_append_f32")
-        nat.check(lib.ipe_attention_f32(buf.q.data_ptr(), k[index].data_ptr(), v[index].data_ptr(),
-                                        buf.attn.data_ptr(), batch, hq, hkv, tokens, capacity, start, stream),
-                  "ipe_attention_f32")
-        nat.check(lib.ipe_gemm_f32(buf.attn.data_ptr(), layer.w_o.data_ptr(), x, rows, h, model.q_rows,
-                                   nat.EPI_RESIDUAL, x, stream), "ipe_gemm_f32 o_proj")
-        nat.check(lib.ipe_rmsnorm(x, layer.post_norm.data_ptr(), buf.h.data_ptr(), rows, h, eps, F32, stream),
-                  "ipe_rmsnorm")
-        nat.check(lib.ipe_gemm_f32(buf.h.data_ptr(), layer.w_gate_up.data_ptr(), buf.act.data_ptr(), rows, 2 * i, h,
-                                   nat.EPI_SILU_MUL, None, stream), "ipe_gemm_f32 gate_up")
-        nat.check(lib.ipe_gemm_f32(buf.act.data_ptr(), layer.w_down.data_ptr(), x, rows, h, i, nat.EPI_RESIDUAL, x,
-                                   stream), "ipe_gemm_f32 down_proj")
+        layer_ops(c, layer, model.q_rows, model.qkv_rows, buf.x, buf.h, buf.qkv, buf.q, buf.attn, buf.act, k[index],
+                  v[index], buf.batch, buf.tokens, start, capacity, cos, sin, stream)
 
 
 def final_norm(model: Fp32Model, x: torch.Tensor, out: torch.Tensor, stream: int) -> torch.Tensor:

@@ -12,8 +12,8 @@ It also builds the bf16 rotary tables the way the reference engine does on the h
 (src/ipe/engine.py:63-67 per position for decode rows; src/ipe/engine.py:78 one call over the
 prompt for prefill).
 
-`prefill_layer` / `decode_layer` issue one decoder layer (src/ipe/forward.py:86-115) as a chain of
-C-ABI launches on the current stream; nothing here computes on the CPU.
+`prefill_ops` / `prefill_layer` issue one decoder layer over a prompt (src/ipe/forward.py:86-115)
+as a chain of C-ABI launches on the current stream; nothing here computes on the CPU.
 """
 
 from __future__ import annotations
@@ -21,6 +21,7 @@ from __future__ import annotations
 import torch
 
 from ipe_b200 import _native as nat
+from ipe_b200 import layer as layer_hook
 from ipe_b200.config import check_supported
 
 
@@ -87,6 +88,7 @@ class PackedModel:
         self.q_rows = c.num_attention_heads * c.head_dim
         self.kv_rows = c.num_key_value_heads * c.head_dim
         self.qkv_rows = self.q_rows + 2 * self.kv_rows
+        layer_hook.register(self, torch.bfloat16)
         self._decode_cos: torch.Tensor | None = None
         self._decode_sin: torch.Tensor | None = None
         self._prefill_tables: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
@@ -147,31 +149,39 @@ class PrefillBuffers:
         self.act = torch.empty((tokens, c.intermediate_size), dtype=bf, device=dev)
 
 
-def prefill_layer(model: PackedModel, index: int, buf: PrefillBuffers, k_layer: torch.Tensor, v_layer: torch.Tensor,
-                  batch: int, length: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor, stream: int) -> None:
-    """One decoder layer over a prompt at positions 0..length-1 (src/ipe/forward.py:86-115, start 0)."""
+def prefill_ops(c, p: dict[str, int], q_rows: int, qkv_rows: int, x: torch.Tensor, h: torch.Tensor, qkv: torch.Tensor,
+                q: torch.Tensor, attn: torch.Tensor, act: torch.Tensor, k_layer: torch.Tensor, v_layer: torch.Tensor,
+                batch: int, length: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor, stream: int) -> None:
+    """One decoder layer over a prompt at positions 0..length-1 (src/ipe/forward.py:86-115, start 0):
+    p holds the packed layer's device pointers; x [batch*length, H] is updated in place."""
     lib = nat.load()
-    c, p = model.config, model.layers[index].ptr
     m = batch * length
-    h, x = buf.h.data_ptr(), buf.x.data_ptr()
+    hp, xp = h.data_ptr(), x.data_ptr()
     eps = c.rms_norm_eps
-    nat.check(lib.ipe_rmsnorm(x, p["in_norm"], h, m, c.hidden_size, eps, 0, stream), "ipe_rmsnorm")
-    nat.check(lib.ipe_gemm(h, p["w_qkv"], buf.qkv.data_ptr(), m, model.qkv_rows, c.hidden_size, nat.EPI_STORE, 0,
-                           stream), "ipe_gemm qkv")
-    nat.check(lib.ipe_qk_norm_rope_append(buf.qkv.data_ptr(), batch, length, c.num_attention_heads,
+    nat.check(lib.ipe_rmsnorm(xp, p["in_norm"], hp, m, c.hidden_size, eps, 0, stream), "ipe_rmsnorm")
+    nat.check(lib.ipe_gemm(hp, p["w_qkv"], qkv.data_ptr(), m, qkv_rows, c.hidden_size, nat.EPI_STORE, 0, stream),
+              "ipe_gemm qkv")
+    nat.check(lib.ipe_qk_norm_rope_append(qkv.data_ptr(), batch, length, c.num_attention_heads,
                                           c.num_key_value_heads, p["q_norm"], p["k_norm"], cos.data_ptr(),
-                                          sin.data_ptr(), 0, None, buf.q.data_ptr(), k_layer.data_ptr(),
+                                          sin.data_ptr(), 0, None, q.data_ptr(), k_layer.data_ptr(),
                                           v_layer.data_ptr(), capacity, eps, stream), "ipe_qk_norm_rope_append")
-    nat.check(lib.ipe_prefill_attention(buf.q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), buf.attn.data_ptr(),
+    nat.check(lib.ipe_prefill_attention(q.data_ptr(), k_layer.data_ptr(), v_layer.data_ptr(), attn.data_ptr(),
                                         batch, c.num_attention_heads, c.num_key_value_heads, length, capacity, stream),
               "ipe_prefill_attention")
-    nat.check(lib.ipe_gemm(buf.attn.data_ptr(), p["w_o"], x, m, c.hidden_size, model.q_rows, nat.EPI_RESIDUAL, x,
-                           stream), "ipe_gemm o_proj")
-    nat.check(lib.ipe_rmsnorm(x, p["post_norm"], h, m, c.hidden_size, eps, 0, stream), "ipe_rmsnorm")
-    nat.check(lib.ipe_gemm(h, p["w_gate_up"], buf.act.data_ptr(), m, 2 * c.intermediate_size, c.hidden_size,
+    nat.check(lib.ipe_gemm(attn.data_ptr(), p["w_o"], xp, m, c.hidden_size, q_rows, nat.EPI_RESIDUAL, xp, stream),
+              "ipe_gemm o_proj")
+    nat.check(lib.ipe_rmsnorm(xp, p["post_norm"], hp, m, c.hidden_size, eps, 0, stream), "ipe_rmsnorm")
+    nat.check(lib.ipe_gemm(hp, p["w_gate_up"], act.data_ptr(), m, 2 * c.intermediate_size, c.hidden_size,
                            nat.EPI_SILU_MUL, 0, stream), "ipe_gemm gate_up")
-    nat.check(lib.ipe_gemm(buf.act.data_ptr(), p["w_down"], x, m, c.hidden_size, c.intermediate_size,
-                           nat.EPI_RESIDUAL, x, stream), "ipe_gemm down_proj")
+    nat.check(lib.ipe_gemm(act.data_ptr(), p["w_down"], xp, m, c.hidden_size, c.intermediate_size,
+                           nat.EPI_RESIDUAL, xp, stream), "ipe_gemm down_proj")
+
+
+def prefill_layer(model: PackedModel, index: int, buf: PrefillBuffers, k_layer: torch.Tensor, v_layer: torch.Tensor,
+                  batch: int, length: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor, stream: int) -> None:
+    """Layer `index` of the packed model over a prompt (prefill_ops on the engine's buffers)."""
+    prefill_ops(model.config, model.layers[index].ptr, model.q_rows, model.qkv_rows, buf.x, buf.h, buf.qkv, buf.q,
+                buf.attn, buf.act, k_layer, v_layer, batch, length, capacity, cos, sin, stream)
 
 
 def run_prefill_layers(model: PackedModel, buf: PrefillBuffers, k: torch.Tensor, v: torch.Tensor, batch: int,
@@ -194,16 +204,7 @@ class DecodeBuffers:
         parts = int(nat.load().ipe_lm_head_parts(c.vocab_size))
         self.parts = parts
         self.partials = torch.empty((parts, batch, nat.PARTIAL_WORDS), dtype=torch.float32, device=dev)
-        ws = int(nat.load().ipe_decode_attention_qkv_workspace(batch, c.num_attention_heads, c.num_key_value_heads,
-                                                                capacity))
-        # split-KV partial records and arrival counters of the fused decode attention (kept zeroed by it)
-        self.workspace = torch.zeros(ws, dtype=torch.uint8, device=dev)
         lib = nat.load()
-        linear = max(int(lib.ipe_decode_linear_workspace(batch, rows, k)) for rows, k in (
-            (model.qkv_rows, c.hidden_size), (c.hidden_size, model.q_rows), (2 * c.intermediate_size, c.hidden_size),
-            (c.hidden_size, c.intermediate_size)))
-        # split-K partial tiles and arrival counters of the decode linear layers (kept zeroed by them)
-        self.linear_workspace = torch.zeros(max(linear, 256), dtype=torch.uint8, device=dev)
         self.state = torch.zeros(nat.STATE_WORDS, dtype=torch.int64, device=dev)
         self.tokens = torch.zeros(batch, dtype=torch.int64, device=dev)
         # generation history: row b, sampled token s at [b, s] (fixed buffers, so captured steps replay)
@@ -212,30 +213,6 @@ class DecodeBuffers:
         step_ws = int(lib.ipe_decode_step_workspace(batch, c.num_attention_heads, c.num_key_value_heads, capacity))
         # grid barrier, attention arrival counters and partial records of the one-kernel decode step
         self.step_workspace = torch.zeros(step_ws, dtype=torch.uint8, device=dev)
-
-
-def decode_layer(model: PackedModel, index: int, buf: DecodeBuffers, k_layer: torch.Tensor, v_layer: torch.Tensor,
-                 batch: int, capacity: int, cos: torch.Tensor, sin: torch.Tensor, stream: int) -> None:
-    """One decoder layer for one token per row at the position in the device step state
-    (src/ipe/forward.py:86-115, start > 0)."""
-    lib = nat.load()
-    c, p = model.config, model.layers[index].ptr
-    x, eps, state = buf.x.data_ptr(), c.rms_norm_eps, buf.state.data_ptr()
-    ws, wsn = buf.linear_workspace.data_ptr(), buf.linear_workspace.numel()
-    nat.check(lib.ipe_rmsnorm_qkv(x, p["in_norm"], p["t_qkv"], buf.qkv.data_ptr(), batch, c.hidden_size,
-                                  model.qkv_rows, eps, ws, wsn, stream), "ipe_rmsnorm_qkv")
-    nat.check(lib.ipe_decode_attention_qkv(buf.qkv.data_ptr(), p["q_norm"], p["k_norm"], cos.data_ptr(),
-                                           sin.data_ptr(), 0, state, k_layer.data_ptr(), v_layer.data_ptr(),
-                                           buf.attn.data_ptr(), batch, c.num_attention_heads, c.num_key_value_heads,
-                                           capacity, eps, buf.workspace.data_ptr(), buf.workspace.numel(), stream),
-              "ipe_decode_attention_qkv")
-    nat.check(lib.ipe_linear_residual(buf.attn.data_ptr(), p["t_o"], x, batch, model.q_rows, c.hidden_size, ws, wsn,
-                                      stream), "ipe_linear_residual o_proj")
-    nat.check(lib.ipe_rmsnorm_gate_up_silu(x, p["post_norm"], p["t_gate_up"], buf.act.data_ptr(), batch,
-                                           c.hidden_size, c.intermediate_size, eps, ws, wsn, stream),
-              "ipe_rmsnorm_gate_up_silu")
-    nat.check(lib.ipe_linear_residual(buf.act.data_ptr(), p["t_down"], x, batch, c.intermediate_size, c.hidden_size,
-                                      ws, wsn, stream), "ipe_linear_residual down_proj")
 
 
 def layer_descs(model: PackedModel, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
