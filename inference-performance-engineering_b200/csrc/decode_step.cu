@@ -5,20 +5,23 @@
 //
 // Why one kernel: every weight byte of the step is known before the step starts, so the weight
 // stream does not depend on activations. Each CTA (one per SM, cooperative launch) has a producer
-// warp that walks its share of ALL phases' decode tiles back to back with bulk copies into
-// per-consumer-warp shared-memory slots and never waits for a phase boundary; ahead of those
-// copies it issues L2 prefetches of the same units, of the K / V rows its attention items will
-// read, and of the norm weights. The 4 consumer warps wait only where the data requires it: at a
-// bounded-spin grid barrier after each phase (the next phase needs the full activation vector),
-// then they stage that vector in shared memory and consume tiles that are usually already there.
+// thread that walks its share of ALL phases' weights back to back and never waits for a phase
+// boundary: a unit's weights are one contiguous run of half tiles (stream_tile.cuh), streamed in
+// 32 KB bulk copies into a ring of shared-memory stages that all four consumer warps read. Copies
+// that large are what lets one SM's copy engine keep up with its share of HBM (8 KB copies cap the
+// whole GPU near 4.9 TB/s, 32 KB ones reach 7.3 TB/s); no weight is prefetched into L2, which
+// only lengthened every L2 round trip. The consumer warps wait only where the data requires it:
+// at a bounded-spin grid barrier after each phase (the next phase needs the full activation
+// vector), then they stage that vector in shared memory and consume stages that are usually
+// already there.
 //
 // Work split: a phase's units (a 32-row block, or a 16-row half block where that evens out the
 // bytes per CTA, always over the whole K: no split-K) are dealt round-robin over the CTAs,
-// continuing where the previous phase stopped; within a CTA a unit's tiles go round-robin to the
-// consumer warps, whose partial sums are reduced in a fixed order through shared memory
+// continuing where the previous phase stopped; within a stage, warp w takes half tiles w and
+// w + 4, and the warps' partial sums are reduced in a fixed order through shared memory
 // (deterministic). Attention runs as (split, KV head, row) items over the CTAs. Every spin (grid
-// barrier, mbarrier) is bounded; a timeout sets the device error word and an abort flag and the
-// kernel winds down.
+// barrier, mbarrier) is bounded; a timeout sets the device error word and an abort flag, the
+// kernel winds down, and the producer waits for its copies in flight before it leaves.
 #include <algorithm>
 #include <cstdlib>
 #include <type_traits>
@@ -34,8 +37,9 @@ namespace ipe {
 namespace {
 
 constexpr int kConsumers = 4;
-constexpr int kMaxSlotsPerWarp = 8;
-constexpr int kMaxStages = kConsumers * kMaxSlotsPerWarp;  // 8 KB slots (bounded by shared memory)
+constexpr int kStageTiles = 8;                             // half tiles per stage (2 per consumer warp)
+constexpr int kStageBytes = kStageTiles * kHalfTileBytes;  // 32 KB: one bulk copy
+constexpr int kMaxStages = 8;
 constexpr int kThreads = 32 * (kConsumers + 1);
 constexpr int kCThreads = 32 * kConsumers;
 constexpr int kPad = 32;
@@ -48,14 +52,13 @@ struct StepArgs {
   int* attn_counters;
   float* attn_records;
   int* err;
-  int slots;                // ring slots per consumer warp
+  int stages;               // 32 KB ring stages
   int max_splits;           // attention splits per (row, KV head)
-  unsigned prefetch_bytes;  // how far the L2 prefetch runs ahead of the shared-memory copies
+  int prefetch_kv;          // the producer prefetches each layer's K / V rows (and norm weights) into L2
   int evict_first;          // weight copies mark their L2 lines evict-first
   int halves;               // half-row-block units allowed
   int act_cols;             // without ACT_SMEM: RMS-normalised phases with K <= act_cols still stage in shared memory
   int bulk_stage;           // with ACT_SMEM: phases without a norm stage their rows by bulk copies (batch > 1)
-  int pair_halves;          // one-GPU step: a ring slot carries two half tiles (t and t + 4) of a half unit
   unsigned xres_off;        // bulk staging: byte offset from the scratch of a copy of the residual rows x (0: none)
   int light_fences;         // grid barrier: acq_rel fence before the arrival, no fence after the acquire load
   int overlap_epilogue;     // warps 1-3 start the next unit while warp 0 runs this unit's epilogue
@@ -333,13 +336,18 @@ __device__ __forceinline__ int first_unit(int cursor) {
 }
 
 // A weight phase as units dealt round-robin over the CTAs: a unit is one row block (32 rows, whole
-// K, 8 KB tiles) or, when that lowers the most bytes any CTA streams in the phase, one 16-row half
-// of a row block (4 KB half tiles).
+// K: its two halves' runs of half tiles, one after the other) or, when that lowers the most bytes
+// any CTA streams in the phase, one 16-row half of a row block (one run).
 struct PhaseShape {
   const unsigned char* tiles;
   int units;
-  int ku;  // tiles per unit
+  int ku;  // k tiles (128 columns) per row
   bool half;
+  __device__ __forceinline__ int half_tiles() const { return half ? ku : 2 * ku; }
+  // the unit's run of half tiles: row block rb, starting at half (u & 1) of a half unit
+  __device__ __forceinline__ const unsigned char* run(int u) const {
+    return tiles + (half ? half_tile_offset(u >> 1, u & 1, 0, ku) : half_tile_offset(u, 0, 0, ku));
+  }
 };
 
 __device__ __forceinline__ PhaseShape make_phase(const void* tiles, int row_blocks, int ku, bool may_halve) {
@@ -371,9 +379,9 @@ struct UnitWalk {
 template <int NT, int G, bool ACT_SMEM, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs a) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
-  const int S = a.slots;
+  const int S = a.stages;
   unsigned char* ring = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(ring + kConsumers * S * kTileBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + static_cast<size_t>(S) * kStageBytes);
   uint64_t* empty = full + kMaxStages;
   float* rstd = reinterpret_cast<float*>(empty + kMaxStages);  // [16]
   int* abort_smem = reinterpret_cast<int*>(rstd + 16);
@@ -387,13 +395,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   const int B = d.batch, H = d.hidden, I = d.intermediate;
   const int Q = d.q_heads * 128, QKV = (d.q_heads + 2 * d.kv_heads) * 128;
   const int G_ = static_cast<int>(gridDim.x);
-  const bool pair_halves = !TP && a.pair_halves != 0;
 
   __shared__ uint64_t stage_bar;  // completion of the bulk copies that stage activation rows
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kConsumers * S; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], kConsumers);
     }
     mbar_init(&stage_bar, 1);
     *abort_smem = 0;
@@ -440,10 +447,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
 
   if (warp == 0) {
     // ------------------------------------------------------------------ producer
-    // Bulk copies of this CTA's tiles into the consumer warps' ring slots (tile t of a unit to
-    // warp t % 4), and, prefetch_bytes ahead of them, L2 prefetches of the same units plus the
-    // K / V rows this CTA's attention items of each layer will read. The per-tile path is kept
-    // short: one thread issues every copy of the SM.
+    // One thread issues every copy of the SM: each unit's run in stages of up to 8 half tiles
+    // (32 KB), one bulk copy per stage, into the ring in order. Entering a layer's QKV phase, it
+    // also prefetches into L2 the K / V rows this CTA's attention items of the layer will read and
+    // the layer's norm weights (they are on the critical path of the next stages and items).
     if (lane == 0) {
       const uint32_t ring_base = smem_addr(ring);
       const uint64_t policy = evict_first_policy();
@@ -452,8 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       const AttnSplit sp = attn_split(pos, a.max_splits);
       auto prefetch_kv = [&](int layer) {
         const ipe_layer_desc& L = d.layer_descs[layer];
-        // the layer's norm weights too (the stages that read them are on the critical path); a
-        // bulk prefetch needs a 16-byte aligned start, so an unaligned vector is left to the loads
+        // a bulk prefetch needs a 16-byte aligned start, so an unaligned vector is left to the loads
         auto prefetch_vec = [&](const void* p, uint32_t bytes) {
           if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) prefetch_l2(p, bytes);
         };
@@ -474,59 +480,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
           }
         }
       };
-      // A unit's tiles are one contiguous range of ku whole tiles (a half unit reads half of each).
-      auto prefetch_unit = [&](const UnitWalk& w) {
-        const int rb = w.ph.half ? w.unit >> 1 : w.unit;
-        const unsigned char* base = w.ph.tiles + static_cast<int64_t>(rb) * w.ph.ku * kTileBytes;
-        for (int t = 0; t < w.ph.ku; t += 8) {  // 8 tiles = 64 KB a prefetch
-          const uint32_t bytes = static_cast<uint32_t>(min(8, w.ph.ku - t)) * kTileBytes;
-          prefetch_l2(base + static_cast<int64_t>(t) * kTileBytes, bytes);
-        }
-      };
-      UnitWalk main_walk, ahead;
-      uint64_t issued = 0, prefetched = 0;
-      SlotCursor sc[kConsumers];
+      UnitWalk walk;
+      SlotCursor rc;  // the ring position of the next copy
       bool ok = true;
       int entered;
-      while (ok && next_unit(main_walk, entered)) {
-        const PhaseShape& ph = main_walk.ph;
-        const uint32_t bytes = ph.half ? kTileBytes / 2 : kTileBytes;
-        while (prefetched < issued + a.prefetch_bytes) {
-          int player;
-          if (!next_unit(ahead, player)) break;
-          if (player >= 0) prefetch_kv(player);
-          prefetch_unit(ahead);
-          prefetched += static_cast<uint64_t>(ahead.ph.ku) * (ahead.ph.half ? kTileBytes / 2 : kTileBytes);
-        }
-        const int rb = ph.half ? main_walk.unit >> 1 : main_walk.unit;
-        const unsigned char* src = ph.tiles + static_cast<int64_t>(rb) * ph.ku * kTileBytes +
-                                   (ph.half ? (main_walk.unit & 1) * (kTileBytes / 2) : 0);
-        // a paired half unit fills each slot with the half tiles t and t + 4 of its warp
-        const bool pair = pair_halves && ph.half;
-        for (int t0 = 0; t0 < ph.ku && ok; t0 += pair ? 2 * kConsumers : kConsumers) {
-#pragma unroll
-          for (int w = 0; w < kConsumers; ++w) {
-            const int t = t0 + w;
-            if (t >= ph.ku || !ok) continue;
-            const bool two = pair && t + kConsumers < ph.ku;
-            const int slot = w * S + sc[w].slot;
-            if (sc[w].fill > 0 && !mbar_wait(&empty[slot], (sc[w].fill - 1) & 1, a.err, a.wait_ns)) {
-              ok = false;
-              continue;
-            }
-            mbar_expect_tx(&full[slot], two ? 2 * bytes : bytes);
-#pragma unroll
-            for (int p = 0; p < 2; ++p) {
-              if (p == 1 && !two) break;
-              const uint32_t dst = ring_base + slot * kTileBytes + p * bytes;
-              const unsigned char* from = src + static_cast<int64_t>(t + p * kConsumers) * kTileBytes;
-              if (a.evict_first) bulk_copy_hint(dst, from, bytes, &full[slot], policy);
-              else bulk_copy(dst, from, bytes, &full[slot]);
-            }
-            sc[w].advance(S);
+      while (ok && next_unit(walk, entered)) {
+        if (entered >= 0 && a.prefetch_kv) prefetch_kv(entered);
+        const PhaseShape& ph = walk.ph;
+        const unsigned char* run = ph.run(walk.unit);
+        const int n_ht = ph.half_tiles();
+        for (int s0 = 0; s0 < n_ht; s0 += kStageTiles) {
+          const uint32_t bytes = static_cast<uint32_t>(min(kStageTiles, n_ht - s0)) * kHalfTileBytes;
+          if (rc.fill > 0 && !mbar_wait(&empty[rc.slot], (rc.fill - 1) & 1, a.err, a.wait_ns)) {
+            ok = false;
+            break;
           }
+          mbar_expect_tx(&full[rc.slot], bytes);
+          const uint32_t dst = ring_base + rc.slot * kStageBytes;
+          const unsigned char* src = run + static_cast<int64_t>(s0) * kHalfTileBytes;
+          if (a.evict_first) bulk_copy_hint(dst, src, bytes, &full[rc.slot], policy);
+          else bulk_copy(dst, src, bytes, &full[rc.slot]);
+          rc.advance(S);
         }
-        issued += static_cast<uint64_t>(ph.ku) * bytes;
+      }
+      // Every copy issued has landed before the thread leaves (on an aborted step the consumers may
+      // have left early): stage s was filled fills(s) times; wait for the last of them.
+      for (int st = 0; st < S; ++st) {
+        const int fills = rc.fill + (st < rc.slot ? 1 : 0);
+        if (fills > 0) mbar_wait(&full[st], (fills - 1) & 1, a.err, a.wait_ns);
       }
     }
     return;
@@ -535,7 +516,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   // -------------------------------------------------------------------- consumers
   const int cw = warp - 1, tid = threadIdx.x - 32;
   const int g = lane >> 2, t = lane & 3;
-  SlotCursor mine;
+  SlotCursor mine;  // the ring position of the next stage (every consumer warp reads every stage)
   int cursor = 0;
   // phase ends so far (each a grid barrier, or in tensor-parallel steps after a row-parallel phase
   // the end of this CTA's pushes), and grid barriers so far
@@ -728,46 +709,65 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
 #pragma unroll
     for (int j = 0; j < NT; ++j) my_rstd[j] = (!smem_act && norm_w && 8 * j + g < B) ? rstd[8 * j + g] : 1.f;
     bool ok = true, first = true;
+    const int n_ht = ph.half_tiles();
     for (int u = first_unit(cursor); u < ph.units; u += G_) {
+      // per half (full unit: half 0, half 1; half unit: [0]) CH independent MMA chains
+      constexpr int CH = NT == 1 ? 4 : 2;
+      float acc4[2][CH][NT][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) acc4[h][c][j][0] = acc4[h][c][j][1] = acc4[h][c][j][2] = acc4[h][c][j][3] = 0.f;
+      for (int s0 = 0; s0 < n_ht && ok; s0 += kStageTiles) {
+        const int slot = mine.slot;
+        const uint32_t base = smem_addr(ring + static_cast<size_t>(slot) * kStageBytes);
+        // this warp's half tiles of the stage are w and w + 4; the first one's activations are
+        // loaded before the wait. Every warp waits for every fill of every stage, with a tile in it
+        // or not, so no warp's parity wait can run a phase ahead of the barrier.
+        uint4 xv[4][NT];
+        const int j0 = s0 + cw;
+        const int h0 = (!ph.half && j0 >= ph.ku) ? 1 : 0;
+        if (j0 < n_ht) load_activations<NT>(xv, (j0 - h0 * ph.ku) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad,
+                                            B, g, t);
+        if (!mbar_wait(&full[slot], mine.fill & 1, a.err, a.wait_ns)) {
+          ok = false;
+          break;
+        }
+        if (trace) {
+          if (first) mark(3);
+          mark(4);
+          first = false;
+        }
+        if (j0 < n_ht) {
+          if (h0 == 0) consume_half_chains<NT, CH>(acc4[0], base + cw * kHalfTileBytes, xv, g, t);
+          else consume_half_chains<NT, CH>(acc4[1], base + cw * kHalfTileBytes, xv, g, t);
+        }
+        const int j1 = j0 + kConsumers;
+        if (j1 < n_ht && j1 < s0 + kStageTiles) {
+          const int h1 = (!ph.half && j1 >= ph.ku) ? 1 : 0;
+          load_activations<NT>(xv, (j1 - h1 * ph.ku) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
+          if (h1 == 0) consume_half_chains<NT, CH>(acc4[0], base + (cw + kConsumers) * kHalfTileBytes, xv, g, t);
+          else consume_half_chains<NT, CH>(acc4[1], base + (cw + kConsumers) * kHalfTileBytes, xv, g, t);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        mine.advance(S);
+      }
+      // the unit's sums per half (half unit: acc[0]), chains added in order
       float acc[2][NT][4];
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
-        for (int j = 0; j < NT; ++j) acc[h][j][0] = acc[h][j][1] = acc[h][j][2] = acc[h][j][3] = 0.f;
-      {
-        // a paired half unit's slot holds this warp's half tiles tt and tt + 4 (the producer's pairing)
-        const bool pair = pair_halves && ph.half;
-        for (int tt = cw; tt < ph.ku && ok; tt += pair ? 2 * kConsumers : kConsumers) {
-          const int slot = cw * S + mine.slot;
-          const uint32_t base = smem_addr(ring + slot * kTileBytes);
-          uint4 xv[4][NT];
-          load_activations<NT>(xv, tt * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
-          if (!mbar_wait(&full[slot], mine.fill & 1, a.err, a.wait_ns)) {
-            ok = false;
-            break;
-          }
-          if (trace) {
-            if (first) mark(3);
-            mark(4);
-            first = false;
-          }
-          if (ph.half) consume_half<NT>(acc, base, xv, g, t);
-          else consume_tile<NT>(acc, base, xv, g, t);
-          if (pair && tt + kConsumers < ph.ku) {
-            load_activations<NT>(xv, (tt + kConsumers) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
-            consume_half<NT>(acc, base + kTileBytes / 2, xv, g, t);
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&empty[slot]);
-          mine.advance(S);
-        }
-      }
-      if (ph.half) {  // the two column chains of a half unit
-#pragma unroll
         for (int j = 0; j < NT; ++j)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) acc[0][j][e] += acc[1][j][e];
-      }
+          for (int e = 0; e < 4; ++e) {
+            float sum = acc4[h][0][j][e];
+#pragma unroll
+            for (int c = 1; c < CH; ++c) sum += acc4[h][c][j][e];
+            acc[h][j][e] = sum;
+          }
       // Fixed-order reduction of the warps' partial sums, then the epilogue by warp 0. Units
       // alternate between two partial-sum buffers, so with overlap_epilogue warps 1-3 go on to the
       // next unit's tiles while warp 0 finishes this one: the barrier after the next unit's
@@ -1026,20 +1026,18 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 }
 
 // Tuning of the weight stream, fixed per process (measured on B200 with Qwen3-1.7B at batch 1, a
-// 512-token context: these defaults gave the shortest step): ring slots per consumer warp
-// (IPE_STEP_SLOTS, 4), the L2 prefetch distance per CTA in KB (IPE_STEP_PREFETCH_KB, 128; larger
-// distances lengthened the latency-bound phases), weight copies marked L2 evict-first
-// (IPE_STEP_EVICT_FIRST, 1), half-row-block units (IPE_STEP_HALF, 1), and two half tiles per ring
-// slot in half-unit phases (IPE_STEP_PAIR, 1: twice the bytes in flight per slot), and bulk-copy
-// staging of the o_proj / down_proj rows with the residual rows beside them (IPE_STEP_BULK, 1), and
-// the grid barrier's lighter fences (IPE_STEP_LIGHT_FENCES, 1), and the unit epilogue overlapped with
-// the next unit's tiles (IPE_STEP_OVERLAP, 1).
+// 512-token context): 32 KB ring stages (IPE_STEP_STAGES, 6, fewer when the activations need the
+// room), the producer's L2 prefetch of each layer's K / V rows and norm weights
+// (IPE_STEP_PREFETCH_KV, 1), weight copies marked L2 evict-first (IPE_STEP_EVICT_FIRST, 1),
+// half-row-block units (IPE_STEP_HALF, 1), bulk-copy staging of the o_proj / down_proj rows with
+// the residual rows beside them (IPE_STEP_BULK, 1), the grid barrier's lighter fences
+// (IPE_STEP_LIGHT_FENCES, 1), and the unit epilogue overlapped with the next unit's tiles
+// (IPE_STEP_OVERLAP, 1).
 struct StepTuning {
-  int slots = 4;
-  unsigned prefetch_kb = 128;
+  int stages = 6;
+  int prefetch_kv = 1;
   int evict_first = 1;
   int halves = 1;
-  int pair = 1;
   int bulk = 1;
   int light_fences = 1;
   int overlap_epilogue = 1;
@@ -1048,11 +1046,10 @@ struct StepTuning {
 const StepTuning& tuning() {
   static const StepTuning t = [] {
     StepTuning r;
-    if (const char* v = std::getenv("IPE_STEP_SLOTS")) r.slots = std::atoi(v);
-    if (const char* v = std::getenv("IPE_STEP_PREFETCH_KB")) r.prefetch_kb = static_cast<unsigned>(std::atoi(v));
+    if (const char* v = std::getenv("IPE_STEP_STAGES")) r.stages = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_PREFETCH_KV")) r.prefetch_kv = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_EVICT_FIRST")) r.evict_first = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_HALF")) r.halves = std::atoi(v);
-    if (const char* v = std::getenv("IPE_STEP_PAIR")) r.pair = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_BULK")) r.bulk = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_LIGHT_FENCES")) r.light_fences = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_OVERLAP")) r.overlap_epilogue = std::atoi(v);
@@ -1061,8 +1058,8 @@ const StepTuning& tuning() {
   return t;
 }
 
-size_t fixed_smem(int nt, int slots) {
-  return 1024 + static_cast<size_t>(kConsumers) * slots * kTileBytes + 2 * kMaxStages * 8 + 16 * 4 + 16 +
+size_t fixed_smem(int nt, int stages) {
+  return 1024 + static_cast<size_t>(stages) * kStageBytes + 2 * kMaxStages * 8 + 16 * 4 + 16 +
          2 * static_cast<size_t>(kConsumers) * 32 * 8 * nt * 4;
 }
 
@@ -1115,7 +1112,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   const size_t act = static_cast<size_t>(d.batch) *
                      (std::max(std::max(d.hidden, d.intermediate), d.q_heads * 128) + kPad) * 2;
   const size_t attn = attn_bytes(group);
-  // Activations stay in shared memory when that leaves room for 4 slots per consumer warp. When
+  // Activations stay in shared memory when that leaves room for 4 ring stages. When
   // the widest rows do not fit (a larger batch), the RMS-normalised phases (QKV, gate/up, the LM
   // head; reduction width `hidden`) still stage theirs if those fit.
   const bool act_smem = fixed_smem(nt, 4) + std::max(act, attn) <= kSmemMax;
@@ -1129,7 +1126,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   a.bulk_stage = tuning().bulk && d.tp_world <= 1 && aligned(d.attn) && aligned(d.act) && d.intermediate % 8 == 0 &&
                  (d.q_heads * 128) % 8 == 0;
   // The residual rows' shared-memory copy (bulk-staged o_proj / down_proj phases), after the scratch
-  // when that still leaves 4 slots per consumer warp.
+  // when that still leaves 4 ring stages.
   a.xres_off = 0;
   const size_t xres_bytes = static_cast<size_t>(d.batch) * d.hidden * 2;
   const size_t scratch16 = (scratch + 15) / 16 * 16;
@@ -1138,16 +1135,15 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
     a.xres_off = static_cast<unsigned>(scratch16);
     scratch = scratch16 + xres_bytes;
   }
-  int slots = std::min(kMaxSlotsPerWarp, std::max(2, tuning().slots));
-  while (slots > 2 && fixed_smem(nt, slots) + scratch > kSmemMax) --slots;
-  a.slots = slots;
-  a.prefetch_bytes = tuning().prefetch_kb * 1024u;
+  int stages = std::min(kMaxStages, std::max(2, tuning().stages));
+  while (stages > 2 && fixed_smem(nt, stages) + scratch > kSmemMax) --stages;
+  a.stages = stages;
+  a.prefetch_kv = tuning().prefetch_kv;
   a.evict_first = tuning().evict_first;
   a.halves = tuning().halves;
-  a.pair_halves = tuning().pair;
   a.light_fences = tuning().light_fences;
   a.overlap_epilogue = tuning().overlap_epilogue;
-  const size_t smem = fixed_smem(nt, slots) + scratch;
+  const size_t smem = fixed_smem(nt, stages) + scratch;
   if (smem > kSmemMax) {
     *message = "decode-step scratch does not fit in shared memory";
     return cudaErrorInvalidValue;

@@ -1,10 +1,8 @@
 // Decode linear layers: persistent, bulk-copy-fed weight-streaming GEMV for 1..16 activation rows.
 //
-// Weight layout ("decode tiles", built once by ipe_decode_tiles): a row block of 32 output rows
-// (for SiLU*up: 16 gate rows then the 16 matching up rows) and 128 columns form one contiguous
-// 8 KB tile: [half (2)][64-column box (2)][row (16)][128 bytes], each 128-byte row segment stored
-// with its 16-byte chunks XOR-swizzled by (row % 8). Tiles run row-block-major, so a row block's
-// K range is one contiguous span of memory.
+// Weight layout ("decode tiles", built once by ipe_decode_tiles, see stream_tile.cuh): 4 KB half
+// tiles of 16 rows x 128 columns stored [row block][half][k tile]. This kernel consumes a row
+// block's two halves of one k tile together: each 8 KB slot is filled by two 4 KB copies.
 //
 // Work: each row block's K range is split into `ksplit` pieces; pieces are dealt in contiguous
 // ranges to one CTA per SM, and within a CTA round-robin to its 4 consumer warps. One producer
@@ -85,18 +83,15 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const GemvArgs
       // Piece p's tiles are p * subs .. p * subs + subs - 1 (a row block's pieces are adjacent), so
       // the walk is pointer arithmetic only: the single issuing thread must stay far ahead. Warp w's
       // k-th tile goes to its slot w * kSlotsPerWarp + k % kSlotsPerWarp as fill k / kSlotsPerWarp.
-      const unsigned char* first = static_cast<const unsigned char*>(a.w) + static_cast<int64_t>(p0) * subs * kTileBytes;
       const uint32_t ring_base = smem_addr(ring);
-      const int64_t piece_bytes = static_cast<int64_t>(subs) * kTileBytes;
+      const int units_per_row = a.k / kSubK;
       bool ok = true;
       for (int q0 = 0, k0 = 0; q0 < npieces && ok; q0 += kConsumers, k0 += subs) {
         const int gs = min(kConsumers, npieces - q0);
-        const unsigned char* group = first + q0 * piece_bytes;
         for (int s = 0; s < subs && ok; ++s) {
           const int k = k0 + s;
           const int fill = k / kSlotsPerWarp, sub = k - fill * kSlotsPerWarp;
-          const unsigned char* src = group + s * kTileBytes;
-          for (int w = 0; w < gs; ++w, src += piece_bytes) {
+          for (int w = 0; w < gs; ++w) {
             const int64_t tile = static_cast<int64_t>(p0 + q0 + w) * subs + s;
             if (tile < 0 || tile >= plan.tiles) {  // never expected: refuse the copy, report
               report(a.err, kErrShape);
@@ -109,7 +104,12 @@ __global__ void __launch_bounds__(kThreads, 2) stream_gemv_kernel(const GemvArgs
               break;
             }
             mbar_expect_tx(&full[slot], kTileBytes);
-            bulk_copy(ring_base + slot * kTileBytes, src, kTileBytes, &full[slot]);
+            const unsigned char* w_base = static_cast<const unsigned char*>(a.w);
+            const int64_t rb = tile / units_per_row, kt = tile % units_per_row;
+            bulk_copy(ring_base + slot * kTileBytes, w_base + half_tile_offset(rb, 0, kt, units_per_row),
+                      kHalfTileBytes, &full[slot]);
+            bulk_copy(ring_base + slot * kTileBytes + kHalfTileBytes, w_base + half_tile_offset(rb, 1, kt, units_per_row),
+                      kHalfTileBytes, &full[slot]);
           }
         }
       }
@@ -314,15 +314,15 @@ __global__ void decode_tiles_kernel(const bf16* __restrict__ w, const bf16* __re
                                     int rows, int k, int64_t chunks) {
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (idx >= chunks) return;
-  // idx = ((((rb * ku_row + ku) * 2 + h) * 2 + j) * 16 + r) * 8 + pc
+  // idx = ((((rb * 2 + h) * ku_row + ku) * 2 + j) * 16 + r) * 8 + pc (half_tile_offset / 16)
   const int pc = static_cast<int>(idx & 7);
   const int r = static_cast<int>((idx >> 3) & 15);
   const int j = static_cast<int>((idx >> 7) & 1);
-  const int h = static_cast<int>((idx >> 8) & 1);
-  const int64_t tile = idx >> 9;
+  const int64_t half_tile = idx >> 8;
   const int ku_row = k / kSubK;
-  const int ku = static_cast<int>(tile % ku_row);
-  const int64_t rb = tile / ku_row;
+  const int ku = static_cast<int>(half_tile % ku_row);
+  const int h = static_cast<int>((half_tile / ku_row) & 1);
+  const int64_t rb = half_tile / ku_row / 2;
   const int lc = pc ^ (r & 7);
   const int col = ku * kSubK + j * 64 + lc * 8;
   int64_t row;

@@ -2,10 +2,15 @@
 // the decode-tile format, bulk copies into shared memory, the tensor-core consumption of one tile,
 // and the linear-layer epilogues with the reference's rounding points.
 //
-// Decode tile: 32 output rows (for SiLU*up: 16 gate rows, then the 16 matching up rows) x 128
-// reduction columns = 8 KB, laid out [half (2)][64-column box (2)][row (16)][128 bytes] with the
-// 16-byte chunks of each 128-byte row segment XOR-swizzled by (row % 8), so that the 16-byte
-// shared-memory reads of a warp are conflict-free. Tiles of one row block are adjacent.
+// Decode tiles: a matrix is cut into row blocks of 32 output rows (for SiLU*up: 16 gate rows, then
+// the 16 matching up rows) and each row block into two 16-row halves. A half tile is 16 rows x 128
+// reduction columns = 4 KB, laid out [64-column box (2)][row (16)][128 bytes] with the 16-byte
+// chunks of each 128-byte row segment XOR-swizzled by (row % 8), so that the 16-byte shared-memory
+// reads of a warp are conflict-free. Half tiles are stored half-major within a row block:
+// [row block][half (2)][k tile (K / 128)][4 KB], so a half's whole reduction range, and a row
+// block's two halves one after the other, are each one contiguous run of memory that streams in a
+// few large bulk copies (a copy's fixed cost makes copies below 16 KB slow: 8 KB copies cap the
+// stream near 4.9 TB/s on B200, 32 KB copies reach 7.3 TB/s).
 #pragma once
 
 #include "common.cuh"
@@ -14,9 +19,15 @@
 
 namespace ipe {
 
-constexpr int kTileBytes = 8192;  // 32 rows x 128 bf16
+constexpr int kTileBytes = 8192;  // a row block's two half tiles of one 128-column range
+constexpr int kHalfTileBytes = 4096;  // 16 rows x 128 bf16
 constexpr int kTileBoxBytes = 2048;  // 16 rows x 64 bf16
 constexpr int kTileK = 128;
+
+// Byte offset of half tile (row block rb, half h, k tile k) in a matrix with ku k tiles per row.
+__host__ __device__ __forceinline__ int64_t half_tile_offset(int64_t rb, int h, int k, int ku) {
+  return ((rb * 2 + h) * ku + k) * static_cast<int64_t>(kHalfTileBytes);
+}
 
 __device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -65,10 +76,11 @@ __device__ __forceinline__ uint64_t evict_first_policy() {
   return policy;
 }
 
-// acc[h][j] += tile rows (h, g / g+8) x activations xv[c][j] (batch columns 8j..8j+7) over the
-// tile's 128 columns. The MMA's K order is permuted identically for A (weights, 16-byte chunk of
-// 8 consecutive columns per thread) and B (activations, the same 8 columns), so the dot products
-// are unchanged while every read is one contiguous 16 bytes.
+// acc[h][j] += rows (h, g / g+8) of a row block's two half tiles for one k tile, gathered at base
+// (half 0) and base + kHalfTileBytes (half 1), x activations xv[c][j] (batch columns 8j..8j+7) over
+// the 128 columns. The MMA's K order is permuted identically for A (weights, 16-byte chunk of 8
+// consecutive columns per thread) and B (activations, the same 8 columns), so the dot products are
+// unchanged while every read is one contiguous 16 bytes.
 template <int NT>
 __device__ __forceinline__ void consume_tile(float (&acc)[2][NT][4], uint32_t base, const uint4 (&xv)[4][NT], int g,
                                              int t) {
@@ -81,7 +93,7 @@ __device__ __forceinline__ void consume_tile(float (&acc)[2][NT][4], uint32_t ba
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int row = g + 8 * r;
-        w[h][r] = lds128(base + (h * 2 + (c >> 1)) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+        w[h][r] = lds128(base + h * kHalfTileBytes + (c >> 1) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
       }
 #pragma unroll
     for (int h = 0; h < 2; ++h)
@@ -112,6 +124,31 @@ __device__ __forceinline__ void consume_half(float (&acc)[2][NT][4], uint32_t ba
     for (int j = 0; j < NT; ++j) {
       mma16816(acc[c >> 1][j], w[0].x, w[1].x, w[0].y, w[1].y, xv[c][j].x, xv[c][j].y);
       mma16816(acc[c >> 1][j], w[0].z, w[1].z, w[0].w, w[1].w, xv[c][j].z, xv[c][j].w);
+    }
+  }
+}
+
+// acc[m % CH][j] += the 16 rows (g / g+8) of one 4 KB half tile at base x activations xv[c][j]
+// over its 128 columns (the same K permutation as consume_tile), the tile's eight MMAs m = 2c + s
+// spread over CH independent accumulator chains: a chain of dependent mma.sync waits out the
+// instruction's latency at every step, so one long chain per warp limits how fast a warp can
+// consume a stage; the caller sums the chains in a fixed order.
+template <int NT, int CH>
+__device__ __forceinline__ void consume_half_chains(float (&acc)[CH][NT][4], uint32_t base, const uint4 (&xv)[4][NT],
+                                                    int g, int t) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int chunk = (c & 1) * 4 + t;
+    uint4 w[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int row = g + 8 * r;
+      w[r] = lds128(base + (c >> 1) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      mma16816(acc[(2 * c) % CH][j], w[0].x, w[1].x, w[0].y, w[1].y, xv[c][j].x, xv[c][j].y);
+      mma16816(acc[(2 * c + 1) % CH][j], w[0].z, w[1].z, w[0].w, w[1].w, xv[c][j].z, xv[c][j].w);
     }
   }
 }

@@ -232,7 +232,7 @@ class Engine:
         token the library sampler on the step's fp32 logits (Gumbel draws keyed by a per-step seed)
         and a decode step on the sampled IDs (src/ipe/engine.py:137-147)."""
         logits = self.prefill(token_ids)
-        device, batch = self._f32.device, self.batch
+        device, batch = self._k.device, self.batch
         tokens = torch.empty((batch, max_new_tokens), dtype=torch.int64, device=device)
         logprobs = torch.empty((batch, max_new_tokens), dtype=torch.float32, device=device)
         stops = torch.tensor(stop_ids, dtype=torch.int64, device=device) if stop_ids else None
