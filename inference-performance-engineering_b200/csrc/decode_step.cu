@@ -329,6 +329,69 @@ __device__ __forceinline__ void load_activations(uint4 (&xv)[4][NT], int k0, boo
     }
 }
 
+// Slot bookkeeping of the ring: stage index and how often it wrapped.
+struct SlotCursor {
+  int slot = 0, fill = 0;
+  __device__ __forceinline__ void advance(int slots) {
+    if (++slot == slots) {
+      slot = 0;
+      ++fill;
+    }
+  }
+};
+
+// The LM head's unit epilogue with one lane per vocabulary row: red holds the four consumer warps'
+// sums in the MMA fragment layout (lane g * 4 + t holds rows h * 16 + g + 8 * (e >> 1), batch column
+// 8 j + 2 t + (e & 1) at [(h * NT + j) * 4 + e]). Per batch row b: lane l adds the warps' sums of row
+// rb * 32 + l in warp order and rounds it to bf16 (the reference's bf16 logits, widened), stores it,
+// and the warp reduces the row block's sampling record (max, sum of exp(l - max), lowest argmax,
+// and with a temperature the Gumbel maximum, its ID and logit) with one exp per lane.
+template <int NT>
+__device__ __forceinline__ void logits_epilogue(const float* red, int rb, int lane, const EpilogueArgs& a) {
+  float* logits = static_cast<float*>(a.out);
+  const float temperature = __int_as_float(static_cast<int>(a.state[IPE_STATE_TEMPERATURE]));
+  const uint64_t seed = static_cast<uint64_t>(a.state[IPE_STATE_SEED]);
+  const int64_t step = a.state[IPE_STATE_STEP];
+  const int h = lane >> 4, g = lane & 7, e_hi = (lane >> 3) & 1;
+  const int n = rb * 32 + lane;
+  const bool live = n < a.rows;
+  for (int b = 0; b < a.batch; ++b) {
+    const int j = b >> 3, t = (b & 7) >> 1, e = 2 * e_hi + (b & 1);
+    const float* src = red + (g * 4 + t) * 8 * NT + (h * NT + j) * 4 + e;
+    float sum = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) sum += src[w * 32 * 8 * NT];
+    const float l = live ? bf16_round(sum) : -INFINITY;
+    if (live) logits[static_cast<int64_t>(b) * a.out_stride + n] = l;
+    const int id = n + a.row_offset;
+    const float m = warp_max(l);
+    const float sx = warp_sum(live ? expf(l - m) : 0.f);
+    int arg = (live && l == m) ? id : 0x7fffffff;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) arg = min(arg, __shfl_xor_sync(0xffffffffu, arg, o));
+    float gs = -INFINITY, gl = 0.f;
+    int garg = 0x7fffffff;
+    if (temperature > 0.f) {
+      const float score = live ? l / temperature - logf(-logf(uniform01(seed, id, b, step))) : -INFINITY;
+      const float best = warp_max(score);
+      garg = (live && score == best) ? id : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) garg = min(garg, __shfl_xor_sync(0xffffffffu, garg, o));
+      gl = __shfl_sync(0xffffffffu, l, (garg - a.row_offset - rb * 32) & 31);
+      gs = best;
+    }
+    if (lane == 0) {
+      float* rec = a.partials + (static_cast<int64_t>(rb) * a.batch + b) * IPE_PARTIAL_WORDS;
+      rec[0] = m;
+      rec[1] = sx;
+      rec[2] = gs;
+      rec[3] = gl;
+      rec[4] = __int_as_float(arg);
+      rec[5] = __int_as_float(garg);
+    }
+  }
+}
+
 // First unit of this CTA in a phase that starts dealing at `cursor`.
 __device__ __forceinline__ int first_unit(int cursor) {
   const int g = static_cast<int>(gridDim.x);
@@ -355,17 +418,6 @@ __device__ __forceinline__ PhaseShape make_phase(const void* tiles, int row_bloc
   const bool half = may_halve && (2 * row_blocks + g - 1) / g < 2 * ((row_blocks + g - 1) / g);
   return {static_cast<const unsigned char*>(tiles), half ? 2 * row_blocks : row_blocks, ku, half};
 }
-
-// Slot bookkeeping of one consumer warp's ring share: slot index and how often it wrapped.
-struct SlotCursor {
-  int slot = 0, fill = 0;
-  __device__ __forceinline__ void advance(int slots) {
-    if (++slot == slots) {
-      slot = 0;
-      ++fill;
-    }
-  }
-};
 
 // Position of a walk over this CTA's units of the step, in stream order.
 struct UnitWalk {
@@ -700,121 +752,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     }
   };
 
-  // One weight phase: this CTA's units, tiles round-robin over the consumer warps.
-  auto run_phase = [&](auto epi_tag, const PhaseShape& ph, const bf16* src, const bf16* norm_w, int K,
-                       const EpilogueArgs& ea) -> bool {
-    constexpr int EPI = decltype(epi_tag)::value;
-    const bool smem_act = act_in_smem(K, norm_w != nullptr);
-    float my_rstd[NT];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) my_rstd[j] = (!smem_act && norm_w && 8 * j + g < B) ? rstd[8 * j + g] : 1.f;
-    bool ok = true, first = true;
-    const int n_ht = ph.half_tiles();
-    for (int u = first_unit(cursor); u < ph.units; u += G_) {
-      // per half (full unit: half 0, half 1; half unit: [0]) CH independent MMA chains
-      constexpr int CH = NT == 1 ? 4 : 2;
-      float acc4[2][CH][NT][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int c = 0; c < CH; ++c)
-#pragma unroll
-          for (int j = 0; j < NT; ++j) acc4[h][c][j][0] = acc4[h][c][j][1] = acc4[h][c][j][2] = acc4[h][c][j][3] = 0.f;
-      for (int s0 = 0; s0 < n_ht && ok; s0 += kStageTiles) {
-        const int slot = mine.slot;
-        const uint32_t base = smem_addr(ring + static_cast<size_t>(slot) * kStageBytes);
-        // this warp's half tiles of the stage are w and w + 4; the first one's activations are
-        // loaded before the wait. Every warp waits for every fill of every stage, with a tile in it
-        // or not, so no warp's parity wait can run a phase ahead of the barrier.
-        uint4 xv[4][NT];
-        const int j0 = s0 + cw;
-        const int h0 = (!ph.half && j0 >= ph.ku) ? 1 : 0;
-        if (j0 < n_ht) load_activations<NT>(xv, (j0 - h0 * ph.ku) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad,
-                                            B, g, t);
-        if (!mbar_wait(&full[slot], mine.fill & 1, a.err, a.wait_ns)) {
-          ok = false;
-          break;
-        }
-        if (trace) {
-          if (first) mark(3);
-          mark(4);
-          first = false;
-        }
-        if (j0 < n_ht) {
-          if (h0 == 0) consume_half_chains<NT, CH>(acc4[0], base + cw * kHalfTileBytes, xv, g, t);
-          else consume_half_chains<NT, CH>(acc4[1], base + cw * kHalfTileBytes, xv, g, t);
-        }
-        const int j1 = j0 + kConsumers;
-        if (j1 < n_ht && j1 < s0 + kStageTiles) {
-          const int h1 = (!ph.half && j1 >= ph.ku) ? 1 : 0;
-          load_activations<NT>(xv, (j1 - h1 * ph.ku) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
-          if (h1 == 0) consume_half_chains<NT, CH>(acc4[0], base + (cw + kConsumers) * kHalfTileBytes, xv, g, t);
-          else consume_half_chains<NT, CH>(acc4[1], base + (cw + kConsumers) * kHalfTileBytes, xv, g, t);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[slot]);
-        mine.advance(S);
-      }
-      // the unit's sums per half (half unit: acc[0]), chains added in order
-      float acc[2][NT][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int j = 0; j < NT; ++j)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            float sum = acc4[h][0][j][e];
-#pragma unroll
-            for (int c = 1; c < CH; ++c) sum += acc4[h][c][j][e];
-            acc[h][j][e] = sum;
-          }
-      // Fixed-order reduction of the warps' partial sums, then the epilogue by warp 0. Units
-      // alternate between two partial-sum buffers, so with overlap_epilogue warps 1-3 go on to the
-      // next unit's tiles while warp 0 finishes this one: the barrier after the next unit's
-      // partials is the one that orders warp 0's reads of this buffer before its reuse.
-      float* red_u = red + (red_flip++ & 1u) * (kConsumers * 32 * 8 * NT);
-      float* part = red_u + (cw * 32 + lane) * 8 * NT;
-#pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int j = 0; j < NT; ++j)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) part[(h * NT + j) * 4 + e] = acc[h][j][e];
-      consumers_sync();
-      if (cw == 0) {
-#pragma unroll
-        for (int w = 1; w < kConsumers; ++w) {
-          const float* other = red_u + (w * 32 + lane) * 8 * NT;
-#pragma unroll
-          for (int h = 0; h < 2; ++h)
-#pragma unroll
-            for (int j = 0; j < NT; ++j)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) acc[h][j][e] += other[(h * NT + j) * 4 + e];
-        }
-        if (EPI == kGemvResidual && tp) {  // a row-parallel layer: push this rank's part
-          if (ph.half) push_parts(acc, u >> 1, u & 1, 1);
-          else push_parts(acc, u, 0, 2);
-        } else if (ph.half) {
-          if constexpr (EPI == kGemvStore || EPI == kGemvResidual)
-            row_block_epilogue<EPI, NT>(acc, u >> 1, lane, ea, u & 1, 1);
-        } else {
-          row_block_epilogue<EPI, NT>(acc, u, lane, ea);
-        }
-      }
-      if (!a.overlap_epilogue) consumers_sync();
-      if (!ok) return false;
-    }
-    if (a.overlap_epilogue) consumers_sync();  // warp 0's last epilogue of the phase is done
-    cursor = (cursor + ph.units) % G_;
-    return true;
-  };
-
-  using EpiStore = std::integral_constant<int, kGemvStore>;
-  using EpiResidual = std::integral_constant<int, kGemvResidual>;
-  using EpiSilu = std::integral_constant<int, kGemvSiluMul>;
-  using EpiLogits = std::integral_constant<int, kGemvLogits>;
-
   bf16* x = static_cast<bf16*>(d.x);
   bf16* qkv = static_cast<bf16*>(d.qkv);
   bf16* attn = static_cast<bf16*>(d.attn);
@@ -825,27 +762,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     return;  // every CTA sees the same position and leaves before the next barrier
   }
   const AttnSplit sp = attn_split(pos, a.max_splits);
-  // o_proj / down_proj epilogues: x += bf16(sum), x read from its shared-memory copy when the
-  // bulk staging brought one
-  EpilogueArgs residual_args{x, H, H, B, nullptr, nullptr, 0.f, 0};
-  if (ACT_SMEM && !TP && a.bulk_stage && a.xres_off != 0) residual_args.res_smem = xres;
+  const bool res_smem = ACT_SMEM && !TP && a.bulk_stage && a.xres_off != 0;
 
-  for (int layer = 0; layer < d.layers; ++layer) {
-    const ipe_layer_desc& L = d.layer_descs[layer];
-    // QKV projection (input RMSNorm fused); tensor parallel: after the previous layer's down_proj
-    // parts, the residual stream moves from x to x_alt
-    if (tp) {
-      if (!stage_tp(x, static_cast<bf16*>(d.x_alt), layer == 0 ? -1 : 1, static_cast<const bf16*>(L.input_layernorm)))
-        return;
-    } else {
-      stage(x, static_cast<const bf16*>(L.input_layernorm), H);
-    }
-    if (!run_phase(EpiStore{}, phase_shape(layer, 0), x, static_cast<const bf16*>(L.input_layernorm), H,
-                   EpilogueArgs{qkv, QKV, QKV, B, nullptr, nullptr, 0.f, 0}))
-      return;
-    if (!phase_end(true)) return;
-    // attention: items (split, KV head, row) over the CTAs
-    {
+  // The step as a sequence of phases, one code path for every weight phase (a single copy of the
+  // tile loop in the kernel, whatever the epilogue): phase p of layer p / 5 is QKV (0), attention
+  // (1), o_proj (2), gate/up (3), down_proj (4); phase 5 * layers is the LM head.
+  const int n_phases = 5 * d.layers + 1;
+  int lm_first = 0;
+  for (int p = 0; p < n_phases; ++p) {
+    const int layer = p / 5, kind = p == 5 * d.layers ? 5 : p % 5;
+    const ipe_layer_desc& L = d.layer_descs[layer < d.layers ? layer : 0];
+    if (kind == 1) {
+      // attention: items (split, KV head, row) over the CTAs
       FusedArgs fa{};
       fa.qkv = qkv;
       fa.q_norm = static_cast<const bf16*>(L.q_norm);
@@ -872,50 +800,160 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
         attention_item<G>(fa, split, rest % d.kv_heads, rest / d.kv_heads, pos, sp, sm, tid);
         mark(4);
       }
+      if (!phase_end(true)) return;
+      continue;
     }
-    if (!phase_end(true)) return;
-    // o_proj + residual (tensor parallel: this rank's part, pushed to every rank)
-    stage(attn, nullptr, Q, x);
-    tp_slot = 0;
-    ++tp_epoch;
-    if (!run_phase(EpiResidual{}, phase_shape(layer, 1), attn, nullptr, Q, residual_args))
-      return;
-    if (!phase_end(!tp)) return;
-    // post-attention RMSNorm + gate/up + SiLU * up (tensor parallel: the residual stream moves back
-    // from x_alt to x with the o_proj parts)
-    if (tp) {
-      if (!stage_tp(static_cast<const bf16*>(d.x_alt), x, 0, static_cast<const bf16*>(L.post_attention_layernorm)))
-        return;
+    // The weight phase's input rows, normalisation, epilogue and whether a grid barrier ends it.
+    // Tensor parallel: the residual stream alternates between x and x_alt around the row-parallel
+    // phases (o_proj, down_proj), whose parts go to every rank and end without a barrier.
+    const bf16* src;
+    const bf16* norm_w;
+    int K, epi;
+    EpilogueArgs ea{x, H, H, B, nullptr, nullptr, 0.f, 0};
+    bool barrier = true;
+    switch (kind) {
+      case 0:
+        src = x, norm_w = static_cast<const bf16*>(L.input_layernorm), K = H, epi = kGemvStore;
+        ea = EpilogueArgs{qkv, QKV, QKV, B, nullptr, nullptr, 0.f, 0};
+        break;
+      case 2:
+        src = attn, norm_w = nullptr, K = Q, epi = kGemvResidual, barrier = !tp;
+        tp_slot = 0;
+        ++tp_epoch;
+        break;
+      case 3:
+        src = x, norm_w = static_cast<const bf16*>(L.post_attention_layernorm), K = H, epi = kGemvSiluMul;
+        ea = EpilogueArgs{act, I, 2 * I, B, nullptr, nullptr, 0.f, 0};
+        break;
+      case 4:
+        src = act, norm_w = nullptr, K = I, epi = kGemvResidual, barrier = !tp;
+        tp_slot = 1;
+        ++tp_epoch;
+        break;
+      default:  // the final RMSNorm + tied LM head: fp32 logits and one sampling record per 32 rows
+        src = x, norm_w = static_cast<const bf16*>(d.final_norm), K = H, epi = kGemvLogits;
+        ea = EpilogueArgs{d.logits, d.vocab, d.vocab, B, d.partials, state, 0.f, 0};
+        ea.row_offset = d.vocab_offset;
+        break;
+    }
+    if (epi == kGemvResidual && res_smem) ea.res_smem = xres;  // x += bf16(sum), x from its staged copy
+    if (tp && norm_w) {
+      const bool ok_stage = kind == 0   ? stage_tp(x, static_cast<bf16*>(d.x_alt), layer == 0 ? -1 : 1, norm_w)
+                            : kind == 3 ? stage_tp(static_cast<const bf16*>(d.x_alt), x, 0, norm_w)
+                                        : stage_tp(x, nullptr, 1, norm_w);
+      if (!ok_stage) return;
+      if (kind == 5) ++tp_epoch;
     } else {
-      stage(x, static_cast<const bf16*>(L.post_attention_layernorm), H);
+      stage(src, norm_w, K, epi == kGemvResidual ? x : nullptr);
     }
-    if (!run_phase(EpiSilu{}, phase_shape(layer, 2), x, static_cast<const bf16*>(L.post_attention_layernorm), H,
-                   EpilogueArgs{act, I, 2 * I, B, nullptr, nullptr, 0.f, 0}))
-      return;
-    if (!phase_end(true)) return;
-    // down_proj + residual (tensor parallel: this rank's part, pushed to every rank)
-    stage(act, nullptr, I, x);
-    tp_slot = 1;
-    ++tp_epoch;
-    if (!run_phase(EpiResidual{}, phase_shape(layer, 3), act, nullptr, I, residual_args))
-      return;
-    if (!phase_end(!tp)) return;
-  }
-  // final RMSNorm + tied LM head: fp32 logits and one sampling record per 32 vocabulary rows, then
-  // one record per row merging this CTA's (tensor parallel: this rank's vocabulary rows, and the
-  // merged records go to every rank)
-  if (tp) {
-    if (!stage_tp(x, nullptr, 1, static_cast<const bf16*>(d.final_norm))) return;
-    ++tp_epoch;
-  } else {
-    stage(x, static_cast<const bf16*>(d.final_norm), H);
+    const PhaseShape ph = phase_shape(layer, kind == 5 ? 0 : kind - (kind > 1 ? 1 : 0));
+    if (kind == 5) lm_first = first_unit(cursor);
+
+    // This CTA's units of the phase; within a stage, warp w takes half tiles w and w + 4.
+    const bool smem_act = act_in_smem(K, norm_w != nullptr);
+    float my_rstd[NT];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) my_rstd[j] = (!smem_act && norm_w && 8 * j + g < B) ? rstd[8 * j + g] : 1.f;
+    bool first = true;
+    const int n_ht = ph.half_tiles();
+    int units_here = 0;
+    for (int u = first_unit(cursor); u < ph.units; u += G_, ++units_here) {
+      // per half (full unit: half 0, half 1; half unit: [0]) CH independent MMA chains
+      constexpr int CH = NT == 1 ? 4 : 2;
+      float acc4[2][CH][NT][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int c = 0; c < CH; ++c)
+#pragma unroll
+          for (int j = 0; j < NT; ++j) acc4[h][c][j][0] = acc4[h][c][j][1] = acc4[h][c][j][2] = acc4[h][c][j][3] = 0.f;
+      for (int s0 = 0; s0 < n_ht; s0 += kStageTiles) {
+        const int slot = mine.slot;
+        const uint32_t base = smem_addr(ring + static_cast<size_t>(slot) * kStageBytes);
+        // this warp's half tiles of the stage are w and w + 4; the first one's activations are
+        // loaded before the wait. Every warp waits for every fill of every stage, with a tile in it
+        // or not, so no warp's parity wait can run a phase ahead of the barrier.
+        uint4 xv[4][NT];
+        const int j0 = s0 + cw;
+        const int h0 = (!ph.half && j0 >= ph.ku) ? 1 : 0;
+        if (j0 < n_ht) load_activations<NT>(xv, (j0 - h0 * ph.ku) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad,
+                                            B, g, t);
+        if (!mbar_wait(&full[slot], mine.fill & 1, a.err, a.wait_ns)) {
+          *abort_smem = 1;  // every warp leaves the phase together, after the barrier below
+          break;
+        }
+        if (trace) {
+          if (first) mark(3);
+          mark(4);
+          first = false;
+        }
+        if (j0 < n_ht) {
+          if (h0 == 0) consume_half_chains<NT, CH>(acc4[0], base + cw * kHalfTileBytes, xv, g, t);
+          else consume_half_chains<NT, CH>(acc4[1], base + cw * kHalfTileBytes, xv, g, t);
+        }
+        const int j1 = j0 + kConsumers;
+        if (j1 < n_ht) {
+          const int h1 = (!ph.half && j1 >= ph.ku) ? 1 : 0;
+          load_activations<NT>(xv, (j1 - h1 * ph.ku) * kTileK, smem_act, xs, src, norm_w, my_rstd, K, kPad, B, g, t);
+          if (h1 == 0) consume_half_chains<NT, CH>(acc4[0], base + (cw + kConsumers) * kHalfTileBytes, xv, g, t);
+          else consume_half_chains<NT, CH>(acc4[1], base + (cw + kConsumers) * kHalfTileBytes, xv, g, t);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);
+        mine.advance(S);
+      }
+      // The warps' sums per half (half unit: [0]) go to shared memory, then one warp adds them in a
+      // fixed order and runs the epilogue: a different warp for each unit (this CTA's k-th unit of
+      // the phase: warp k % 4), so that no warp falls behind the others by more than one epilogue
+      // (every stage waits for all four). Units alternate between two partial-sum buffers; with
+      // overlap_epilogue the other warps go on to the next unit's stages meanwhile, and the barrier
+      // after the next unit's partials orders the epilogue's reads of this buffer before its reuse.
+      float* red_u = red + (red_flip++ & 1u) * (kConsumers * 32 * 8 * NT);
+      {
+        float* part = red_u + (cw * 32 + lane) * 8 * NT;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int j = 0; j < NT; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float sum = acc4[h][0][j][e];
+#pragma unroll
+              for (int c = 1; c < CH; ++c) sum += acc4[h][c][j][e];
+              part[(h * NT + j) * 4 + e] = sum;
+            }
+      }
+      consumers_sync();
+      if (*abort_smem != 0) return;
+      if (cw == units_here % kConsumers && epi == kGemvLogits) {
+        logits_epilogue<NT>(red_u, u, lane, ea);
+      } else if (cw == units_here % kConsumers) {
+        float acc[2][NT][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int j = 0; j < NT; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float sum = 0.f;
+#pragma unroll
+              for (int w = 0; w < kConsumers; ++w) sum += red_u[(w * 32 + lane) * 8 * NT + (h * NT + j) * 4 + e];
+              acc[h][j][e] = sum;
+            }
+        const int rb = ph.half ? u >> 1 : u, first_half = ph.half ? (u & 1) : 0, halves = ph.half ? 1 : 2;
+        if (epi == kGemvResidual && tp) push_parts(acc, rb, first_half, halves);  // this rank's part
+        else if (epi == kGemvStore) row_block_epilogue<kGemvStore, NT>(acc, rb, lane, ea, first_half, halves);
+        else if (epi == kGemvResidual) row_block_epilogue<kGemvResidual, NT>(acc, rb, lane, ea, first_half, halves);
+        else row_block_epilogue<kGemvSiluMul, NT>(acc, rb, lane, ea);
+      }
+      if (!a.overlap_epilogue) consumers_sync();
+    }
+    if (a.overlap_epilogue) consumers_sync();  // the last epilogue of the phase is done
+    cursor = (cursor + ph.units) % G_;
+    if (kind != 5 && !phase_end(barrier)) return;
   }
   {
     const PhaseShape lm = phase_shape(d.layers, 0);
-    const int lm_first = first_unit(cursor);
-    EpilogueArgs ea{d.logits, d.vocab, d.vocab, B, d.partials, state, 0.f, 0};
-    ea.row_offset = d.vocab_offset;
-    if (!run_phase(EpiLogits{}, lm, x, static_cast<const bf16*>(d.final_norm), H, ea)) return;
     // rows over the consumer warps; this CTA's units lane-strided, then the lanes in a fixed tree
     for (int b = cw; b < B; b += kConsumers) {
       Stat st = empty_stat();

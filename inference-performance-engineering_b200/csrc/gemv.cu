@@ -323,7 +323,7 @@ __global__ void decode_tiles_kernel(const bf16* __restrict__ w, const bf16* __re
   const int ku = static_cast<int>(half_tile % ku_row);
   const int h = static_cast<int>((half_tile / ku_row) & 1);
   const int64_t rb = half_tile / ku_row / 2;
-  const int lc = pc ^ (r & 7);
+  const int lc = swizzle(pc, r);  // the logical chunk stored at physical chunk pc (self-inverse)
   const int col = ku * kSubK + j * 64 + lc * 8;
   int64_t row;
   const bf16* src;

@@ -4,9 +4,10 @@
 //
 // Decode tiles: a matrix is cut into row blocks of 32 output rows (for SiLU*up: 16 gate rows, then
 // the 16 matching up rows) and each row block into two 16-row halves. A half tile is 16 rows x 128
-// reduction columns = 4 KB, laid out [64-column box (2)][row (16)][128 bytes] with the 16-byte
-// chunks of each 128-byte row segment XOR-swizzled by (row % 8), so that the 16-byte shared-memory
-// reads of a warp are conflict-free. Half tiles are stored half-major within a row block:
+// reduction columns = 4 KB, laid out [64-column box (2)][row (16)][128 bytes]; in odd rows the two
+// 64-byte halves of each 128-byte row segment are swapped (16-byte chunk c stored at c ^ 4). The
+// consumers' 16-byte loads are served 8 lanes at a time: lanes (row 2p or 2p + 1, chunk t of a
+// 64-byte half) then cover all 32 banks once, with no bank conflict. Half tiles are stored half-major within a row block:
 // [row block][half (2)][k tile (K / 128)][4 KB], so a half's whole reduction range, and a row
 // block's two halves one after the other, are each one contiguous run of memory that streams in a
 // few large bulk copies (a copy's fixed cost makes copies below 16 KB slow: 8 KB copies cap the
@@ -23,6 +24,9 @@ constexpr int kTileBytes = 8192;  // a row block's two half tiles of one 128-col
 constexpr int kHalfTileBytes = 4096;  // 16 rows x 128 bf16
 constexpr int kTileBoxBytes = 2048;  // 16 rows x 64 bf16
 constexpr int kTileK = 128;
+
+// Stored position of 16-byte chunk `chunk` (0..7) of a tile row: odd rows swap their 64-byte halves.
+__host__ __device__ __forceinline__ int swizzle(int chunk, int row) { return chunk ^ ((row & 1) << 2); }
 
 // Byte offset of half tile (row block rb, half h, k tile k) in a matrix with ku k tiles per row.
 __host__ __device__ __forceinline__ int64_t half_tile_offset(int64_t rb, int h, int k, int ku) {
@@ -93,7 +97,7 @@ __device__ __forceinline__ void consume_tile(float (&acc)[2][NT][4], uint32_t ba
 #pragma unroll
       for (int r = 0; r < 2; ++r) {
         const int row = g + 8 * r;
-        w[h][r] = lds128(base + h * kHalfTileBytes + (c >> 1) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+        w[h][r] = lds128(base + h * kHalfTileBytes + (c >> 1) * kTileBoxBytes + row * 128 + (swizzle(chunk, row) << 4));
       }
 #pragma unroll
     for (int h = 0; h < 2; ++h)
@@ -118,7 +122,7 @@ __device__ __forceinline__ void consume_half(float (&acc)[2][NT][4], uint32_t ba
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int row = g + 8 * r;
-      w[r] = lds128(base + (c >> 1) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+      w[r] = lds128(base + (c >> 1) * kTileBoxBytes + row * 128 + (swizzle(chunk, row) << 4));
     }
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
@@ -143,7 +147,7 @@ __device__ __forceinline__ void consume_half_chains(float (&acc)[CH][NT][4], uin
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       const int row = g + 8 * r;
-      w[r] = lds128(base + (c >> 1) * kTileBoxBytes + row * 128 + ((chunk ^ (row & 7)) << 4));
+      w[r] = lds128(base + (c >> 1) * kTileBoxBytes + row * 128 + (swizzle(chunk, row) << 4));
     }
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
