@@ -197,7 +197,9 @@ size_t ipe_decode_attention_workspace(int batch, int q_heads, int capacity);
  * 0..position, and the merge of the chunks by the last chunk block of each (row, KV head).
  *   qkv bf16 [batch, (q_heads + 2*kv_heads) * 128] -> out bf16 [batch, q_heads * 128]
  * workspace: ipe_decode_attention_qkv_workspace bytes, zero-filled before first use (its arrival
- * counters return to zero after every call). Replaces src/ipe/forward.py:101-112 for a decode step
+ * counters return to zero after every call). The caches and the workspace must be 16-byte aligned
+ * (K / V rows and the split records move by bulk copies into shared memory), else
+ * IPE_ERR_ARGUMENT. Replaces src/ipe/forward.py:101-112 for a decode step
  * (qk_norm, apply_rotary, cache write, ops.attention). */
 int ipe_decode_attention_qkv(const void* qkv, const void* q_norm_weight, const void* k_norm_weight,
                              const void* cos_table, const void* sin_table, int start,
@@ -313,7 +315,8 @@ typedef struct {
 typedef struct {
   int layers, hidden, intermediate, q_heads, kv_heads, vocab, capacity, batch;
   float eps;
-  const ipe_layer_desc* layer_descs; /* device array of `layers` descriptors                 */
+  const ipe_layer_desc* layer_descs; /* device array of `layers` descriptors (16-byte aligned;
+                                        copied into shared memory once per step)             */
   const void* embed;                 /* bf16 [vocab, hidden], row-major (the input embedding) */
   const void* lm_head_tiles;         /* decode tiles of the (tied) LM head                    */
   const void* final_norm;            /* bf16 [hidden]                                         */

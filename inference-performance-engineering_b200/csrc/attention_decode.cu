@@ -158,7 +158,13 @@ __global__ void __launch_bounds__(128) decode_combine_kernel(const float* __rest
 // Fused decode-step attention (decode_attention.cuh): one CTA per (split, KV head, batch row).
 template <int G>
 __global__ void __launch_bounds__(kAttnThreads) fused_decode_kernel(const FusedArgs a) {
-  extern __shared__ float scratch[];
+  extern __shared__ __align__(16) float scratch[];
+  __shared__ uint64_t bars[kAttnSlotsMax + 1];
+  if (threadIdx.x == 0) {
+    attn_ring_init(bars);
+    fence_barrier_init();
+  }
+  __syncthreads();
   pdl_trigger();
   pdl_wait();
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -169,7 +175,8 @@ __global__ void __launch_bounds__(kAttnThreads) fused_decode_kernel(const FusedA
   }
   const AttnSplit sp = attn_split(pos, a.max_splits);
   if (split >= sp.splits) return;
-  attention_item<G>(a, split, kvh, b, pos, sp, AttnSmem<G>(scratch), threadIdx.x);
+  AttnSeq seq;
+  attention_item<G>(a, split, kvh, b, pos, sp, AttnSmem<G>(scratch, bars, kAttnSlotsMax), seq, threadIdx.x);
 }
 
 template <int G>
@@ -214,7 +221,7 @@ size_t fused_decode_workspace_bytes(int batch, int q_heads, int kv_heads, int ca
 
 template <int G>
 cudaError_t launch_fused(const FusedArgs& a, int batch, cudaStream_t stream) {
-  const size_t smem = static_cast<size_t>(attn_smem_floats<G>()) * sizeof(float);
+  const size_t smem = static_cast<size_t>(attn_smem_floats<G>(kAttnSlotsMax)) * sizeof(float);
   auto kernel = fused_decode_kernel<G>;
   if (smem > 40 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -241,7 +248,7 @@ cudaError_t launch_decode_attention_fused(const void* qkv, const void* q_norm, c
   a.q_heads = q_heads;
   a.kv_heads = kv_heads;
   a.capacity = capacity;
-  a.max_splits = attn_max_splits(2 * sm_count(), batch, kv_heads);
+  a.max_splits = std::min(attn_max_splits(2 * sm_count(), batch, kv_heads), attn_merge_splits(q_heads / kv_heads, kAttnSlotsMax));
   a.eps = eps;
   a.err = err;
   a.counters = static_cast<int*>(workspace);

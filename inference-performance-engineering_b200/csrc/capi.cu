@@ -342,6 +342,8 @@ int ipe_decode_attention_qkv(const void* qkv, const void* q_norm_weight, const v
   const size_t need = ipe::fused_decode_workspace_bytes(batch, q_heads, kv_heads, capacity);
   if (!workspace || workspace_bytes < need)
     return fail(IPE_ERR_ARGUMENT, "ipe_decode_attention_qkv: a zero-filled workspace of %zu bytes is needed", need);
+  if (!aligned16(k_cache) || !aligned16(v_cache) || !aligned16(workspace))
+    return fail(IPE_ERR_ARGUMENT, "ipe_decode_attention_qkv: caches and workspace must be 16-byte aligned (bulk copies)");
   return cuda_status(ipe::launch_decode_attention_fused(qkv, q_norm_weight, k_norm_weight, cos_table, sin_table, state,
                                                         start, k_cache, v_cache, out, batch, q_heads, kv_heads,
                                                         capacity, eps, workspace, device_error_word(),
@@ -501,7 +503,8 @@ int ipe_decode_step(const ipe_decode_step_desc* d, void* stream) {
       !d->workspace)
     return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: null pointer in the descriptor");
   const void* const operands[] = {d->embed, d->lm_head_tiles, d->final_norm, d->cos_table, d->sin_table, d->x,
-                                  d->qkv,   d->attn,          d->act,        d->logits,    d->workspace};
+                                  d->qkv,   d->attn,          d->act,        d->logits,    d->workspace,
+                                  d->layer_descs};
   for (const void* p : operands)
     if (!aligned16(p)) return fail(IPE_ERR_ARGUMENT, "ipe_decode_step: descriptor pointers must be 16-byte aligned");
   if (d->layers < 1 || d->batch < 1 || d->batch > 16 || d->capacity < 1 || d->vocab < 1 || d->q_heads < 1 ||

@@ -5,11 +5,14 @@
 // The item normalises (q_norm) and rotates this step's query heads of the group straight from the
 // QKV projection output; the split that holds the current position also normalises / rotates the
 // step's key and appends K and V to the cache (its own scores read the new key from shared
-// memory). Keys stream in 32-key sub-chunks whose K and V rows are loaded one sub-chunk ahead into
-// registers; an fp32 online softmax carries the running max and sum across sub-chunks. A single
-// split writes the output directly; with several, each writes a partial record (unnormalised o,
-// max, sum) and the last split of each (row, KV head) to arrive (an atomic counter it resets)
-// merges all records in split order, so the result does not depend on arrival order.
+// memory). Keys stream in 32-key sub-chunks: thread 0 bulk-copies each sub-chunk's K and V rows
+// (16 KB) into a ring of up to kAttnSlotsMax shared-memory slots, all of them in flight from the
+// item's start, so the sub-chunks wait on one L2 round trip between them at most instead of one
+// each; an fp32 online softmax carries the running max and sum across sub-chunks. A single split
+// writes the output directly; with several, each writes a partial record (unnormalised o, max,
+// sum) and the last split of each (row, KV head) to arrive (an atomic counter it resets) copies
+// every split's record into the free ring in one bulk copy per head and merges them in split
+// order, so the result does not depend on arrival order.
 #pragma once
 
 #include "common.cuh"
@@ -18,7 +21,10 @@ namespace ipe {
 
 constexpr int kAttnChunk = 32;                       // keys per sub-chunk
 constexpr int kAttnThreads = 128;                    // threads per item
-constexpr int kAttnRecord = 128 + 2;                 // floats per record: o[128], max, sum
+constexpr int kAttnRecord = 128 + 4;                 // floats per record: o[128], max, sum, 2 unused (528 bytes)
+constexpr int kAttnSlotBytes = 2 * kAttnChunk * 128 * 2;  // one ring slot: a sub-chunk's K rows, then its V rows
+constexpr int kAttnSlotsMax = 4;                      // ring slots at most
+constexpr int kAttnSlotsMin = 2;  // at least: a slot is refilled one sub-chunk after it was read
 constexpr int kAttnSplitsMax = 32;                   // splits per (row, KV head) at most
 constexpr float kAttnScale = 0.08838834764831845f;  // 128 ** -0.5
 constexpr int kAttnBarrier = 2;                      // named barrier id used by an item
@@ -39,6 +45,7 @@ struct FusedArgs {
   int q_heads, kv_heads, capacity, max_splits;
   float eps;
   int* err;
+  uint64_t wait_ns;  // bound of every mbarrier wait (0: kWaitLimitNs)
   uint64_t* trace;  // nullable: this item's milestones go to trace[0] (q ready, first K / V requested) and trace[1] (P.V done)
 };
 
@@ -59,27 +66,54 @@ __host__ __device__ inline int attn_max_splits(int ctas, int batch, int kv_heads
   return s < 1 ? 1 : (s > kAttnSplitsMax ? kAttnSplitsMax : s);
 }
 
-// Shared-memory scratch of one item: floats, see attn_smem_floats.
+// Splits a merge can take: every split's record of the G heads fits in the ring of `slots` slots.
+__host__ __device__ constexpr int attn_merge_splits(int group, int slots) {
+  return slots * kAttnSlotBytes / (group * kAttnRecord * 4) < kAttnSplitsMax
+             ? slots * kAttnSlotBytes / (group * kAttnRecord * 4)
+             : kAttnSplitsMax;
+}
+
+// Shared-memory scratch of one item (16-byte aligned base): the ring, then floats, see
+// attn_smem_floats. The ring's mbarriers live outside the scratch (the scratch is shared with
+// other phases of the decode-step kernel): `bars` holds kAttnSlotsMax + 1 of them, one per slot
+// and one for the merge's copies, each initialised with an arrival count of 1 (attn_ring_init).
 template <int G>
 struct AttnSmem {
-  float* qs;      // [G][128]
-  float* sc;      // [2][G][kAttnChunk]
-  float* red;     // [8][G][128]
-  float* stat;    // [G][2] running max, sum
-  float* alpha;   // [G] rescale of this sub-chunk
-  float* knew;    // [128] this step's key (normalised, rotated, bf16 values)
-  float* vnew;    // [128] this step's value
-  float* weight;  // [G][kAttnSplitsMax]
+  unsigned char* ring;  // [slots][kAttnSlotBytes]
+  float* qs;            // [G][128]
+  float* sc;            // [2][G][kAttnChunk]
+  float* red;           // [8][G][128]
+  float* stat;          // [G][2] running max, sum
+  float* alpha;         // [G] rescale of this sub-chunk
+  float* knew;          // [128] this step's key (normalised, rotated, bf16 values)
+  float* vnew;          // [128] this step's value
+  float* weight;        // [G][kAttnSplitsMax]
   int* last;
-  __device__ explicit AttnSmem(float* base)
-      : qs(base), sc(qs + G * 128), red(sc + 2 * G * kAttnChunk), stat(red + 8 * G * 128), alpha(stat + 2 * G),
-        knew(alpha + G), vnew(knew + 128), weight(vnew + 128),
-        last(reinterpret_cast<int*>(weight + G * kAttnSplitsMax)) {}
+  uint64_t* bars;
+  int slots;
+  __device__ AttnSmem(float* base, uint64_t* bars_, int slots_)
+      : ring(reinterpret_cast<unsigned char*>(base)), qs(base + slots_ * (kAttnSlotBytes / 4)), sc(qs + G * 128),
+        red(sc + 2 * G * kAttnChunk), stat(red + 8 * G * 128), alpha(stat + 2 * G), knew(alpha + G),
+        vnew(knew + 128), weight(vnew + 128), last(reinterpret_cast<int*>(weight + G * kAttnSplitsMax)),
+        bars(bars_), slots(slots_) {}
 };
 
 template <int G>
-__host__ __device__ constexpr int attn_smem_floats() {
-  return G * 128 + 2 * G * kAttnChunk + 8 * G * 128 + 3 * G + 256 + G * kAttnSplitsMax + 4;
+__host__ __device__ constexpr int attn_smem_floats(int slots) {
+  return slots * (kAttnSlotBytes / 4) + G * 128 + 2 * G * kAttnChunk + 8 * G * 128 + 3 * G + 256 +
+         G * kAttnSplitsMax + 4;
+}
+
+// Ring fills and merges of this CTA so far: the parities of the next waits. Every thread of the
+// item keeps its own copy, updated identically.
+struct AttnSeq {
+  uint32_t fills = 0, merges = 0;
+};
+
+// Thread 0 initialises the ring's mbarriers; the caller then orders the initialisation before use
+// (fence_barrier_init and a CTA barrier).
+__device__ __forceinline__ void attn_ring_init(uint64_t* bars) {
+  for (int i = 0; i <= kAttnSlotsMax; ++i) mbar_init(&bars[i], 1);
 }
 
 __device__ __forceinline__ void attn_sync() {
@@ -114,30 +148,14 @@ __device__ __forceinline__ void norm_rope4(float (&x)[4], const bf16* w, const f
   }
 }
 
-// K rows for the score layout (key c0 + 8 warp + lane/4, dims 32 (lane%4) ..) and V rows for the
-// P.V layout (keys c0 + tid/16 + 8j, dims 8 (tid%16) ..) of the sub-chunk at c0. Keys at or past
-// `end` and the key at `pos` (not yet in the cache) are not loaded.
-__device__ __forceinline__ void load_kv(const bf16* k_head, const bf16* v_head, int c0, int end, int pos, int tid,
-                                        uint4 (&kr)[4], uint4 (&vr)[4]) {
-  const int warp = tid >> 5, lane = tid & 31;
-  const int key = c0 + warp * 8 + (lane >> 2);
-  const bool kin = key < end && key != pos;
-#pragma unroll
-  for (int v = 0; v < 4; ++v)
-    kr[v] = kin ? ldcg16(k_head + static_cast<int64_t>(key) * 128 + (lane & 3) * 32 + v * 8) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int kv = c0 + (tid >> 4) + 8 * j;
-    vr[j] = kv < end && kv != pos ? ldcg16(v_head + static_cast<int64_t>(kv) * 128 + (tid & 15) * 8)
-                                  : make_uint4(0, 0, 0, 0);
-  }
-}
-
-// One item. tid in [0, 128). pos: this step's position (length = pos + 1); sp from attn_split;
-// split < sp.splits. Every thread of the item must call it.
+// One item. tid in [0, 128). pos: this step's position (length = pos + 1); sp from attn_split with
+// sp.splits <= attn_merge_splits(G, s.slots); split < sp.splits; s.slots >= kAttnSlotsMin (slot
+// (i - 1) % slots is refilled with sub-chunk i - 1 + slots after the scores of sub-chunk i, so
+// sub-chunk i was issued before anyone waits for it only with two slots or more). Every thread of the item must call
+// it, with the same seq. The K / V cache rows must be 16-byte aligned (bulk copies).
 template <int G>
 __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, int pos, AttnSplit sp,
-                               const AttnSmem<G>& s, int tid) {
+                               const AttnSmem<G>& s, AttnSeq& seq, int tid) {
   const int warp = tid >> 5, lane = tid & 31;
   const int begin = split * sp.span;
   const int end = min(begin + sp.span, pos + 1);
@@ -147,9 +165,39 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
   const bf16* k_head = a.k_cache + head_base * 128;
   const bf16* v_head = a.v_cache + head_base * 128;
   const bool appends = end == pos + 1;
+  const uint64_t wait_ns = a.wait_ns ? a.wait_ns : kWaitLimitNs;
+  if (s.slots < kAttnSlotsMin || sp.splits > attn_merge_splits(G, s.slots) ||
+      ((reinterpret_cast<uintptr_t>(a.k_cache) | reinterpret_cast<uintptr_t>(a.v_cache)) & 15u)) {
+    // host checks keep this from happening (the decode step's caches come from device descriptors)
+    if (tid == 0) report(a.err, kErrShape);
+    return;
+  }
 
-  // Everything this item reads first, issued together: q (and, appending, k / v) rows, this
-  // position's cos / sin, and the first sub-chunk of K and V.
+  // The K / V ring: sub-chunk i of the split (keys begin + 32 i ..) goes to slot (fills + i) % slots.
+  // Only keys already in the cache are copied (the appended key is read from shared memory); rows
+  // of a slot past them hold stale values that the scores mask and P.V skips.
+  const int nsub = (end - begin + kAttnChunk - 1) / kAttnChunk;
+  const int cached_end = appends ? pos : end;
+  const uint32_t ring = smem_addr(s.ring);
+  auto issue = [&](int i) {  // thread 0
+    const uint32_t n = seq.fills + static_cast<uint32_t>(i);
+    const int slot = static_cast<int>(n % static_cast<uint32_t>(s.slots));
+    const int c0 = begin + i * kAttnChunk;
+    const int rows = max(0, min(c0 + kAttnChunk, cached_end) - c0);
+    const uint32_t bytes = static_cast<uint32_t>(rows) * 256u;
+    mbar_expect_tx(&s.bars[slot], 2u * bytes);
+    if (rows > 0) {
+      const uint32_t dst = ring + static_cast<uint32_t>(slot) * kAttnSlotBytes;
+      bulk_copy(dst, k_head + static_cast<int64_t>(c0) * 128, bytes, &s.bars[slot]);
+      bulk_copy(dst + kAttnSlotBytes / 2, v_head + static_cast<int64_t>(c0) * 128, bytes, &s.bars[slot]);
+    }
+  };
+  // (a caller whose threads wrote this scratch before has them fence the async proxy first)
+  if (tid == 0)
+    for (int i = 0; i < min(s.slots, nsub); ++i) issue(i);
+
+  // Everything else this item reads first, issued together: q (and, appending, k / v) rows and
+  // this position's cos / sin.
   uint2 qraw[(G + 3) / 4];
 #pragma unroll
   for (int i = 0; i < (G + 3) / 4; ++i) {
@@ -162,8 +210,6 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
   float cs[4], sn[4];
   unpack4(*reinterpret_cast<const uint2*>(a.cos_t + static_cast<int64_t>(pos) * 128 + lane * 4), cs);
   unpack4(*reinterpret_cast<const uint2*>(a.sin_t + static_cast<int64_t>(pos) * 128 + lane * 4), sn);
-  uint4 kr[4], vr[4];
-  load_kv(k_head, v_head, begin, end, pos, tid, kr, vr);
 
 #pragma unroll
   for (int i = 0; i < (G + 3) / 4; ++i) {
@@ -203,12 +249,16 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
 #pragma unroll
     for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
 
-  int buf = 0;
-  for (int c0 = begin; c0 < end; c0 += kAttnChunk, buf ^= 1) {
-    uint4 kn[4], vn[4];
-    if (c0 + kAttnChunk < end) load_kv(k_head, v_head, c0 + kAttnChunk, end, pos, tid, kn, vn);
-    float* sc = s.sc + buf * G * kAttnChunk;
-    // Scores: 4 lanes per key, 32 dims per lane.
+  for (int i = 0; i < nsub; ++i) {
+    const int c0 = begin + i * kAttnChunk;
+    const uint32_t n = seq.fills + static_cast<uint32_t>(i);
+    const uint32_t slot = n % static_cast<uint32_t>(s.slots);
+    mbar_wait(&s.bars[slot], (n / static_cast<uint32_t>(s.slots)) & 1u, a.err, wait_ns);
+    const unsigned char* ks = s.ring + slot * kAttnSlotBytes;
+    const unsigned char* vs = ks + kAttnSlotBytes / 2;
+    float* sc = s.sc + (i & 1) * G * kAttnChunk;
+    // Scores: 4 lanes per key, 32 dims per lane, read as four 16-byte pieces in a rotated order
+    // that gives the 8 lanes of each quarter-warp 8 different bank groups (key rows are 256 bytes).
     {
       const int kk = warp * 8 + (lane >> 2);
       const int part = lane & 3;
@@ -218,17 +268,18 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
       for (int g = 0; g < G; ++g) dot[g] = 0.f;
 #pragma unroll
       for (int v = 0; v < 4; ++v) {
+        const int vv = (v + (part >> 1) + 2 * (kk & 1)) & 3;
         float f[8];
         if (key == pos) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i) f[i] = s.knew[part * 32 + v * 8 + i];
+          for (int e = 0; e < 8; ++e) f[e] = s.knew[part * 32 + vv * 8 + e];
         } else {
-          unpack8(kr[v], f);
+          unpack8(*reinterpret_cast<const uint4*>(ks + kk * 256 + part * 64 + vv * 16), f);
         }
 #pragma unroll
         for (int g = 0; g < G; ++g)
 #pragma unroll
-          for (int i = 0; i < 8; ++i) dot[g] += f[i] * s.qs[g * 128 + part * 32 + v * 8 + i];
+          for (int e = 0; e < 8; ++e) dot[g] += f[e] * s.qs[g * 128 + part * 32 + vv * 8 + e];
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
@@ -241,6 +292,8 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
       }
     }
     attn_sync();
+    // every thread is past its P.V reads of sub-chunk i - 1: its slot takes sub-chunk i - 1 + slots
+    if (tid == 0 && i >= 1 && i - 1 + s.slots < nsub) issue(i - 1 + s.slots);
     // Online softmax per head: running max / sum, this sub-chunk's probabilities and rescale.
     for (int g = warp; g < G; g += kAttnThreads / 32) {
       const float sv = sc[g * kAttnChunk + lane];
@@ -257,37 +310,34 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
       }
     }
     attn_sync();
-    // P.V: thread (key group kg, dims 8 dc ..), keys kg + 8j.
+    // P.V: thread (key group kg, dims 8 dc ..), keys kg + 8j; keys past the split are skipped.
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float al = s.alpha[g];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) o[g][i] *= al;
+      for (int e = 0; e < 8; ++e) o[g][e] *= al;
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int kk = kg + 8 * j;
       const int key = c0 + kk;
+      if (key >= end) continue;
       float f[8];
       if (key == pos) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) f[i] = s.vnew[dc * 8 + i];
+        for (int e = 0; e < 8; ++e) f[e] = s.vnew[dc * 8 + e];
       } else {
-        unpack8(vr[j], f);
+        unpack8(*reinterpret_cast<const uint4*>(vs + kk * 256 + dc * 16), f);
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float p = sc[g * kAttnChunk + kk];  // 0 past the end
+        const float p = sc[g * kAttnChunk + kk];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[g][i] += p * f[i];
+        for (int e = 0; e < 8; ++e) o[g][e] += p * f[e];
       }
     }
-#pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      kr[v] = kn[v];
-      vr[v] = vn[v];
-    }
   }
+  seq.fills += static_cast<uint32_t>(nsub);
 #pragma unroll
   for (int g = 0; g < G; ++g)
 #pragma unroll
@@ -322,27 +372,38 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
   }
   // Arrival: the last split of this (row, KV head) merges every split. The records written by
   // every thread are ordered before thread 0's acq_rel fence by the barrier (release); the last
-  // arriver's fence after its counter update orders the merge's reads after it (acquire), and the
-  // barrier passes that on to the other threads.
+  // arriver's fence after its counter update orders its reads after it (acquire), and the proxy
+  // fence extends that to its bulk copies of the records into the ring (free again: every thread
+  // is past its last P.V read).
   attn_sync();
+  const int S = sp.splits;
+  const uint32_t head_bytes = static_cast<uint32_t>(S) * kAttnRecord * 4u;
+  const float* rec0 = a.records + (static_cast<int64_t>(b) * a.q_heads + kvh * G) * kAttnSplitsMax * kAttnRecord;
   if (tid == 0) {
     int* counter = a.counters + b * a.kv_heads + kvh;
     asm volatile("fence.acq_rel.gpu;" ::: "memory");
     const int prior = atomicAdd(counter, 1);
-    *s.last = prior == sp.splits - 1;
+    *s.last = prior == S - 1;
     if (*s.last) {
       *counter = 0;
       asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      asm volatile("fence.proxy.async.global;" ::: "memory");
+      mbar_expect_tx(&s.bars[kAttnSlotsMax], static_cast<uint32_t>(G) * head_bytes);
+      for (int g = 0; g < G; ++g)
+        bulk_copy(ring + g * head_bytes, rec0 + static_cast<int64_t>(g) * kAttnSplitsMax * kAttnRecord, head_bytes,
+                  &s.bars[kAttnSlotsMax]);
     }
   }
   attn_sync();
   if (!*s.last) return;
+  mbar_wait(&s.bars[kAttnSlotsMax], seq.merges & 1u, a.err, wait_ns);
+  ++seq.merges;
+  const float* R = reinterpret_cast<const float*>(s.ring);  // [G][S][kAttnRecord]
   // Per head (one lane per split): weights exp(m_s - M) / L, then every thread sums its dims.
   for (int g = warp; g < G; g += kAttnThreads / 32) {
-    const float* base = a.records + (static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * kAttnSplitsMax * kAttnRecord;
-    const bool in = lane < sp.splits;
-    const float ms = in ? __ldcg(base + lane * kAttnRecord + 128) : -INFINITY;
-    const float ls = in ? __ldcg(base + lane * kAttnRecord + 129) : 0.f;
+    const bool in = lane < S;
+    const float ms = in ? R[(g * S + lane) * kAttnRecord + 128] : -INFINITY;
+    const float ls = in ? R[(g * S + lane) * kAttnRecord + 129] : 0.f;
     const float m = warp_max(ms);
     const float e = in ? expf(ms - m) : 0.f;
     const float l = warp_sum(ls * e);
@@ -351,17 +412,10 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
   attn_sync();
   for (int i = tid; i < G * 128; i += kAttnThreads) {
     const int g = i / 128, d = i % 128;
-    const float* base = a.records + (static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * kAttnSplitsMax * kAttnRecord;
     const float* wg = s.weight + g * kAttnSplitsMax;
+    const float* rg = R + g * S * kAttnRecord + d;
     float acc = 0.f;
-    for (int c0 = 0; c0 < sp.splits; c0 += 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = c0 + u < sp.splits ? __ldcg(base + (c0 + u) * kAttnRecord + d) : 0.f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (c0 + u < sp.splits) acc += wg[c0 + u] * v[u];
-    }
+    for (int c = 0; c < S; ++c) acc += wg[c] * rg[c * kAttnRecord];
     a.out[(static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * 128 + d] = __float2bfloat16_rn(acc);
   }
   attn_sync();  // the item's shared scratch may be reused right after

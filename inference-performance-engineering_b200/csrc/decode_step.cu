@@ -54,7 +54,9 @@ struct StepArgs {
   int* err;
   int stages;               // 32 KB ring stages
   int max_splits;           // attention splits per (row, KV head)
+  int attn_slots;           // attention K / V ring slots (16 KB each, at the start of the scratch)
   int prefetch_kv;          // the producer prefetches each layer's K / V rows (and norm weights) into L2
+  int l2_ahead;             // the producer keeps this many stages past its copies prefetched into L2
   int evict_first;          // weight copies mark their L2 lines evict-first
   int halves;               // half-row-block units allowed
   int act_cols;             // without ACT_SMEM: RMS-normalised phases with K <= act_cols still stage in shared memory
@@ -426,6 +428,13 @@ struct UnitWalk {
   PhaseShape ph{};
 };
 
+// Position of a walk over this CTA's ring stages of the step (up to 32 KB of one unit's run each).
+struct StageWalk {
+  UnitWalk w;
+  const unsigned char* run = nullptr;
+  int n_ht = 0, s0 = 0;
+};
+
 // TP: a tensor-parallel rank (tp_world > 1; needs ACT_SMEM), compiled apart so that the one-GPU
 // variants carry none of its code.
 template <int NT, int G, bool ACT_SMEM, bool TP>
@@ -438,7 +447,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   float* rstd = reinterpret_cast<float*>(empty + kMaxStages);  // [16]
   int* abort_smem = reinterpret_cast<int*>(rstd + 16);
   float* red = reinterpret_cast<float*>(abort_smem + 4);  // [2 units][kConsumers][32][8 * NT]
-  float* scratch = red + 2 * kConsumers * 32 * 8 * NT;    // activations or attention scratch
+  // the layer descriptors, copied once: every phase reads its operands' addresses from here
+  ipe_layer_desc* descs = reinterpret_cast<ipe_layer_desc*>(red + 2 * kConsumers * 32 * 8 * NT);
+  float* scratch = reinterpret_cast<float*>(descs + a.d.layers);  // activations or attention scratch (16-byte aligned)
   bf16* xres = reinterpret_cast<bf16*>(reinterpret_cast<unsigned char*>(scratch) + a.xres_off);  // if xres_off
   bf16* xs = reinterpret_cast<bf16*>(scratch);
 
@@ -449,21 +460,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   const int G_ = static_cast<int>(gridDim.x);
 
   __shared__ uint64_t stage_bar;  // completion of the bulk copies that stage activation rows
+  __shared__ uint64_t attn_bars[kAttnSlotsMax + 1];  // the attention items' K / V ring and merge copies
+  __shared__ uint64_t desc_bar;                      // completion of the layer descriptors' copy
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kConsumers);
     }
     mbar_init(&stage_bar, 1);
+    attn_ring_init(attn_bars);
+    mbar_init(&desc_bar, 1);
     *abort_smem = 0;
     fence_barrier_init();
   }
   __syncthreads();
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = static_cast<uint32_t>(a.d.layers) * sizeof(ipe_layer_desc);
+    mbar_expect_tx(&desc_bar, bytes);
+    bulk_copy(smem_addr(descs), a.d.layer_descs, bytes, &desc_bar);
+  }
 
   // kind: 0 QKV, 1 o_proj, 2 gate/up, 3 down_proj; layer == layers: the LM head.
   auto phase_shape = [&](int layer, int kind) -> PhaseShape {
     if (layer == d.layers) return make_phase(d.lm_head_tiles, (d.vocab + 31) / 32, H / kTileK, false);
-    const ipe_layer_desc& L = d.layer_descs[layer];
+    const ipe_layer_desc& L = descs[layer];
     switch (kind) {
       case 0: return make_phase(L.qkv_tiles, QKV / 32, H / kTileK, a.halves != 0);
       case 1: return make_phase(L.o_tiles, H / 32, Q / kTileK, a.halves != 0);
@@ -507,10 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       const uint32_t ring_base = smem_addr(ring);
       const uint64_t policy = evict_first_policy();
       const int pos = static_cast<int>(d.state[IPE_STATE_POS]);
-      if (pos < 0 || pos >= d.capacity) return;  // the consumers leave too; nothing was issued
+      // the descriptors' copy (this thread issued it) lands before anything reads them or it leaves
+      if (!mbar_wait(&desc_bar, 0, a.err, a.wait_ns)) atomicExch(&a.grid_bar[1], 1u);
+      if (pos < 0 || pos >= d.capacity) return;  // the consumers leave too; nothing else was issued
       const AttnSplit sp = attn_split(pos, a.max_splits);
       auto prefetch_kv = [&](int layer) {
-        const ipe_layer_desc& L = d.layer_descs[layer];
+        const ipe_layer_desc& L = descs[layer];
         // a bulk prefetch needs a 16-byte aligned start, so an unaligned vector is left to the loads
         auto prefetch_vec = [&](const void* p, uint32_t bytes) {
           if ((reinterpret_cast<uintptr_t>(p) & 15u) == 0) prefetch_l2(p, bytes);
@@ -532,6 +554,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
           }
         }
       };
+      // The L2 window: stages past the ring's copies are prefetched into L2, a.l2_ahead of them, so
+      // that HBM keeps streaming while the ring is full and the consumers wait at a phase boundary;
+      // the copies then read those stages from L2 (and mark them evict-first).
+      StageWalk pf;
+      auto prefetch_next = [&]() {
+        while (pf.s0 >= pf.n_ht) {
+          int entered_pf;
+          if (!next_unit(pf.w, entered_pf)) return;
+          pf.run = pf.w.ph.run(pf.w.unit);
+          pf.n_ht = pf.w.ph.half_tiles();
+          pf.s0 = 0;
+        }
+        const uint32_t bytes = static_cast<uint32_t>(min(kStageTiles, pf.n_ht - pf.s0)) * kHalfTileBytes;
+        prefetch_l2(pf.run + static_cast<int64_t>(pf.s0) * kHalfTileBytes, bytes);
+        pf.s0 += kStageTiles;
+      };
+      for (int i = 0; i < a.l2_ahead; ++i) prefetch_next();
       UnitWalk walk;
       SlotCursor rc;  // the ring position of the next copy
       bool ok = true;
@@ -553,6 +592,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
           if (a.evict_first) bulk_copy_hint(dst, src, bytes, &full[rc.slot], policy);
           else bulk_copy(dst, src, bytes, &full[rc.slot]);
           rc.advance(S);
+          if (a.l2_ahead > 0) prefetch_next();
         }
       }
       // Every copy issued has landed before the thread leaves (on an aborted step the consumers may
@@ -763,7 +803,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   }
   const AttnSplit sp = attn_split(pos, a.max_splits);
   const bool res_smem = ACT_SMEM && !TP && a.bulk_stage && a.xres_off != 0;
+  AttnSeq attn_seq;  // the attention ring's fills and merges so far (the same in every consumer thread)
 
+  if (!mbar_wait(&desc_bar, 0, a.err, a.wait_ns)) {
+    atomicExch(&a.grid_bar[1], 1u);  // every CTA leaves at its next barrier
+    *abort_smem = 1;
+  }
   // The step as a sequence of phases, one code path for every weight phase (a single copy of the
   // tile loop in the kernel, whatever the epilogue): phase p of layer p / 5 is QKV (0), attention
   // (1), o_proj (2), gate/up (3), down_proj (4); phase 5 * layers is the LM head.
@@ -771,7 +816,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   int lm_first = 0;
   for (int p = 0; p < n_phases; ++p) {
     const int layer = p / 5, kind = p == 5 * d.layers ? 5 : p % 5;
-    const ipe_layer_desc& L = d.layer_descs[layer < d.layers ? layer : 0];
+    const ipe_layer_desc& L = descs[layer < d.layers ? layer : 0];
     if (kind == 1) {
       // attention: items (split, KV head, row) over the CTAs
       FusedArgs fa{};
@@ -791,13 +836,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       fa.max_splits = a.max_splits;
       fa.eps = d.eps;
       fa.err = a.err;
+      fa.wait_ns = a.wait_ns;
       const int items = sp.splits * d.kv_heads * B;
-      const AttnSmem<G> sm(scratch);
+      const AttnSmem<G> sm(scratch, attn_bars, a.attn_slots);
       for (int it = static_cast<int>(blockIdx.x); it < items; it += G_) {
         const int split = it % sp.splits, rest = it / sp.splits;
         // the first item's milestones: K / V requested and q ready, scores and P.V done, merged
         fa.trace = trace && it == static_cast<int>(blockIdx.x) ? trace + 1 + 5 * (barrier_index - 1) + 2 : nullptr;
-        attention_item<G>(fa, split, rest % d.kv_heads, rest / d.kv_heads, pos, sp, sm, tid);
+        attention_item<G>(fa, split, rest % d.kv_heads, rest / d.kv_heads, pos, sp, sm, attn_seq, tid);
         mark(4);
       }
       if (!phase_end(true)) return;
@@ -950,6 +996,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
     }
     if (a.overlap_epilogue) consumers_sync();  // the last epilogue of the phase is done
     cursor = (cursor + ph.units) % G_;
+    // the attention ring's bulk copies overwrite the scratch this phase staged: every thread's
+    // generic writes of it go before them
+    if (kind == 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     if (kind != 5 && !phase_end(barrier)) return;
   }
   {
@@ -1069,8 +1118,9 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // (IPE_STEP_PREFETCH_KV, 1), weight copies marked L2 evict-first (IPE_STEP_EVICT_FIRST, 1),
 // half-row-block units (IPE_STEP_HALF, 1), bulk-copy staging of the o_proj / down_proj rows with
 // the residual rows beside them (IPE_STEP_BULK, 1), the grid barrier's lighter fences
-// (IPE_STEP_LIGHT_FENCES, 1), and the unit epilogue overlapped with the next unit's tiles
-// (IPE_STEP_OVERLAP, 1).
+// (IPE_STEP_LIGHT_FENCES, 1), the unit epilogue overlapped with the next unit's tiles
+// (IPE_STEP_OVERLAP, 1), and the attention items' K / V ring slots at most (IPE_STEP_ATTN_SLOTS, 4;
+// as many as fit beside the weight stages).
 struct StepTuning {
   int stages = 6;
   int prefetch_kv = 1;
@@ -1079,6 +1129,8 @@ struct StepTuning {
   int bulk = 1;
   int light_fences = 1;
   int overlap_epilogue = 1;
+  int attn_slots = 4;
+  int l2_ahead = 0;
 };
 
 const StepTuning& tuning() {
@@ -1091,22 +1143,27 @@ const StepTuning& tuning() {
     if (const char* v = std::getenv("IPE_STEP_BULK")) r.bulk = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_LIGHT_FENCES")) r.light_fences = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_OVERLAP")) r.overlap_epilogue = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_ATTN_SLOTS")) r.attn_slots = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_L2_AHEAD")) r.l2_ahead = std::atoi(v);
     return r;
   }();
   return t;
 }
 
-size_t fixed_smem(int nt, int stages) {
+// The dynamic shared memory before the scratch: alignment slack, the ring, its barriers, the RMS
+// scales, the abort flag, the partial sums and the layer descriptors.
+size_t fixed_smem(int nt, int stages, int layers) {
   return 1024 + static_cast<size_t>(stages) * kStageBytes + 2 * kMaxStages * 8 + 16 * 4 + 16 +
-         2 * static_cast<size_t>(kConsumers) * 32 * 8 * nt * 4;
+         2 * static_cast<size_t>(kConsumers) * 32 * 8 * nt * 4 + static_cast<size_t>(layers) * sizeof(ipe_layer_desc);
 }
+static_assert(sizeof(ipe_layer_desc) % 16 == 0, "layer descriptors keep the scratch 16-byte aligned");
 
-size_t attn_bytes(int group) {
+size_t attn_bytes(int group, int slots) {
   switch (group) {
-    case 1: return attn_smem_floats<1>() * 4;
-    case 2: return attn_smem_floats<2>() * 4;
-    case 4: return attn_smem_floats<4>() * 4;
-    default: return attn_smem_floats<8>() * 4;
+    case 1: return attn_smem_floats<1>(slots) * 4;
+    case 2: return attn_smem_floats<2>(slots) * 4;
+    case 4: return attn_smem_floats<4>(slots) * 4;
+    default: return attn_smem_floats<8>(slots) * 4;
   }
 }
 
@@ -1136,7 +1193,6 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   a.d = d;
   a.err = err;
   a.wait_ns = d.wait_limit_ns > 0 ? static_cast<uint64_t>(d.wait_limit_ns) : kWaitLimitNs;
-  a.max_splits = attn_max_splits(sm_count(), d.batch, d.kv_heads);
   unsigned char* ws = static_cast<unsigned char*>(d.workspace);
   a.grid_bar = reinterpret_cast<unsigned*>(ws);
   a.attn_counters = reinterpret_cast<int*>(ws + 256);
@@ -1149,39 +1205,48 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   const int group = d.q_heads / d.kv_heads;
   const size_t act = static_cast<size_t>(d.batch) *
                      (std::max(std::max(d.hidden, d.intermediate), d.q_heads * 128) + kPad) * 2;
-  const size_t attn = attn_bytes(group);
+  const size_t attn1 = attn_bytes(group, kAttnSlotsMin);
   // Activations stay in shared memory when that leaves room for 4 ring stages. When
   // the widest rows do not fit (a larger batch), the RMS-normalised phases (QKV, gate/up, the LM
   // head; reduction width `hidden`) still stage theirs if those fit.
-  const bool act_smem = fixed_smem(nt, 4) + std::max(act, attn) <= kSmemMax;
+  const bool act_smem = fixed_smem(nt, 4, d.layers) + std::max(act, attn1) <= kSmemMax;
   const size_t act_h = static_cast<size_t>(d.batch) * (d.hidden + kPad) * 2;
-  const bool act_h_smem = !act_smem && fixed_smem(nt, 4) + std::max(act_h, attn) <= kSmemMax;
-  size_t scratch = act_smem ? std::max(act, attn) : act_h_smem ? std::max(act_h, attn) : attn;
+  const bool act_h_smem = !act_smem && fixed_smem(nt, 4, d.layers) + std::max(act_h, attn1) <= kSmemMax;
   a.act_cols = act_h_smem ? d.hidden : 0;
   // Bulk staging copies whole rows of the attention output and the SiLU product: 16-byte aligned
   // buffers and widths.
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   a.bulk_stage = tuning().bulk && d.tp_world <= 1 && aligned(d.attn) && aligned(d.act) && d.intermediate % 8 == 0 &&
                  (d.q_heads * 128) % 8 == 0;
-  // The residual rows' shared-memory copy (bulk-staged o_proj / down_proj phases), after the scratch
-  // when that still leaves 4 ring stages.
-  a.xres_off = 0;
+  // The scratch: the activation rows or the attention scratch (whichever is larger), then, with
+  // bulk-staged o_proj / down_proj phases, a copy of the residual rows when that still leaves 4
+  // ring stages.
+  const size_t act_part = act_smem ? act : act_h_smem ? act_h : 0;
   const size_t xres_bytes = static_cast<size_t>(d.batch) * d.hidden * 2;
-  const size_t scratch16 = (scratch + 15) / 16 * 16;
-  if (act_smem && a.bulk_stage && aligned(d.x) && d.hidden % 8 == 0 &&
-      fixed_smem(nt, 4) + scratch16 + xres_bytes <= kSmemMax) {
-    a.xres_off = static_cast<unsigned>(scratch16);
-    scratch = scratch16 + xres_bytes;
-  }
+  auto round16 = [](size_t v) { return (v + 15) / 16 * 16; };
+  auto base_scratch = [&](int slots) { return std::max(act_part, attn_bytes(group, slots)); };
+  const bool xres = act_smem && a.bulk_stage && aligned(d.x) && d.hidden % 8 == 0 &&
+                    fixed_smem(nt, 4, d.layers) + round16(base_scratch(kAttnSlotsMin)) + xres_bytes <= kSmemMax;
+  auto scratch_with = [&](int slots) { return xres ? round16(base_scratch(slots)) + xres_bytes : base_scratch(slots); };
   int stages = std::min(kMaxStages, std::max(2, tuning().stages));
-  while (stages > 2 && fixed_smem(nt, stages) + scratch > kSmemMax) --stages;
+  while (stages > 2 && fixed_smem(nt, stages, d.layers) + scratch_with(kAttnSlotsMin) > kSmemMax) --stages;
   a.stages = stages;
+  // The attention ring (kAttnSlotsMin slots at least) grows into what the weight stages leave.
+  int slots = kAttnSlotsMin;
+  while (slots < std::min(kAttnSlotsMax, std::max(kAttnSlotsMin, tuning().attn_slots)) &&
+         fixed_smem(nt, stages, d.layers) + scratch_with(slots + 1) <= kSmemMax)
+    ++slots;
+  a.attn_slots = slots;
+  a.max_splits = std::min(attn_max_splits(sm_count(), d.batch, d.kv_heads), attn_merge_splits(group, slots));
+  a.xres_off = xres ? static_cast<unsigned>(round16(base_scratch(slots))) : 0u;
+  const size_t scratch = scratch_with(slots);
   a.prefetch_kv = tuning().prefetch_kv;
+  a.l2_ahead = std::max(0, std::min(64, tuning().l2_ahead));
   a.evict_first = tuning().evict_first;
   a.halves = tuning().halves;
   a.light_fences = tuning().light_fences;
   a.overlap_epilogue = tuning().overlap_epilogue;
-  const size_t smem = fixed_smem(nt, stages) + scratch;
+  const size_t smem = fixed_smem(nt, stages, d.layers) + scratch;
   if (smem > kSmemMax) {
     *message = "decode-step scratch does not fit in shared memory";
     return cudaErrorInvalidValue;

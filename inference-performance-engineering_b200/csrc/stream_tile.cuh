@@ -52,27 +52,6 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-__device__ __forceinline__ void bulk_copy(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-               "l"(src), "r"(bytes), "r"(smem_addr(bar))
-               : "memory");
-}
-
-// The same copy with an L2 eviction-priority policy (from createpolicy) on the source lines.
-__device__ __forceinline__ void bulk_copy_hint(uint32_t dst, const void* src, uint32_t bytes, uint64_t* bar,
-                                               uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
-          dst),
-      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
-      : "memory");
-}
-
-// Asynchronous prefetch of [src, src + bytes) into L2 (16-byte aligned, a multiple of 16 bytes).
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
 // L2 policy that evicts the lines it covers first (data read once).
 __device__ __forceinline__ uint64_t evict_first_policy() {
   uint64_t policy;
