@@ -4,15 +4,19 @@
 //
 // The item normalises (q_norm) and rotates this step's query heads of the group straight from the
 // QKV projection output; the split that holds the current position also normalises / rotates the
-// step's key and appends K and V to the cache (its own scores read the new key from shared
-// memory). Keys stream in 32-key sub-chunks: thread 0 bulk-copies each sub-chunk's K and V rows
-// (16 KB) into a ring of up to kAttnSlotsMax shared-memory slots, all of them in flight from the
-// item's start, so the sub-chunks wait on one L2 round trip between them at most instead of one
-// each; an fp32 online softmax carries the running max and sum across sub-chunks. A single split
-// writes the output directly; with several, each writes a partial record (unnormalised o, max,
-// sum) and the last split of each (row, KV head) to arrive (an atomic counter it resets) copies
-// every split's record into the free ring in one bulk copy per head and merges them in split
-// order, so the result does not depend on arrival order.
+// step's key and appends K and V to the cache, and writes them into its last sub-chunk's rows.
+// Keys stream in 32-key sub-chunks: every thread copies its share of each sub-chunk's K and V rows
+// (16 KB, 16-byte cp.async into XOR-swizzled 256-byte rows) into a ring of up to kAttnSlotsMax
+// shared-memory slots, all of them in flight from the item's start. Both products run on the
+// tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate, the G query heads as the 8-wide N):
+// scores S = K q^T from ldmatrix fragments of the key rows; P.V as O^T = V^T P^T from transposed
+// ldmatrix fragments of the value rows, with P split into two bf16 terms (high part and the
+// remainder) so its fp32 value carries over to about 16 significant bits. An fp32 online softmax
+// carries the running max and sum across sub-chunks. A single split writes the output directly;
+// with several, each writes a partial record (unnormalised o, max, sum) and the last split of each
+// (row, KV head) to arrive (an atomic counter it resets) copies every split's record into the free
+// ring in one bulk copy per head and merges them in split order, so the result does not depend on
+// arrival order.
 #pragma once
 
 #include "common.cuh"
@@ -76,32 +80,31 @@ __host__ __device__ constexpr int attn_merge_splits(int group, int slots) {
 // Shared-memory scratch of one item (16-byte aligned base): the ring, then floats, see
 // attn_smem_floats. The ring's mbarriers live outside the scratch (the scratch is shared with
 // other phases of the decode-step kernel): `bars` holds kAttnSlotsMax + 1 of them, one per slot
-// and one for the merge's copies, each initialised with an arrival count of 1 (attn_ring_init).
+// (an arrival per thread of the item and fill) and one for the merge's bulk copies (attn_ring_init).
+// A slot holds a sub-chunk's 32 K rows, then its 32 V rows, 256 bytes each; the 16-byte chunk c of
+// row r sits at chunk c ^ (r & 7) (ring_offset), so the 8 rows one ldmatrix matrix reads at the
+// same columns fall in 8 different bank groups.
 template <int G>
 struct AttnSmem {
-  unsigned char* ring;  // [slots][kAttnSlotBytes]
+  unsigned char* ring;  // [slots][2][kAttnChunk][256 bytes]
   float* qs;            // [G][128]
   float* sc;            // [2][G][kAttnChunk]
-  float* red;           // [8][G][128]
   float* stat;          // [G][2] running max, sum
   float* alpha;         // [G] rescale of this sub-chunk
-  float* knew;          // [128] this step's key (normalised, rotated, bf16 values)
-  float* vnew;          // [128] this step's value
   float* weight;        // [G][kAttnSplitsMax]
   int* last;
   uint64_t* bars;
   int slots;
   __device__ AttnSmem(float* base, uint64_t* bars_, int slots_)
       : ring(reinterpret_cast<unsigned char*>(base)), qs(base + slots_ * (kAttnSlotBytes / 4)), sc(qs + G * 128),
-        red(sc + 2 * G * kAttnChunk), stat(red + 8 * G * 128), alpha(stat + 2 * G), knew(alpha + G),
-        vnew(knew + 128), weight(vnew + 128), last(reinterpret_cast<int*>(weight + G * kAttnSplitsMax)),
+        stat(sc + 2 * G * kAttnChunk), alpha(stat + 2 * G), weight(alpha + G),
+        last(reinterpret_cast<int*>(weight + G * kAttnSplitsMax)),
         bars(bars_), slots(slots_) {}
 };
 
 template <int G>
 __host__ __device__ constexpr int attn_smem_floats(int slots) {
-  return slots * (kAttnSlotBytes / 4) + G * 128 + 2 * G * kAttnChunk + 8 * G * 128 + 3 * G + 256 +
-         G * kAttnSplitsMax + 4;
+  return slots * (kAttnSlotBytes / 4) + G * 128 + 2 * G * kAttnChunk + 3 * G + G * kAttnSplitsMax + 4;
 }
 
 // Ring fills and merges of this CTA so far: the parities of the next waits. Every thread of the
@@ -113,7 +116,13 @@ struct AttnSeq {
 // Thread 0 initialises the ring's mbarriers; the caller then orders the initialisation before use
 // (fence_barrier_init and a CTA barrier).
 __device__ __forceinline__ void attn_ring_init(uint64_t* bars) {
-  for (int i = 0; i <= kAttnSlotsMax; ++i) mbar_init(&bars[i], 1);
+  for (int i = 0; i < kAttnSlotsMax; ++i) mbar_init(&bars[i], kAttnThreads);
+  mbar_init(&bars[kAttnSlotsMax], 1);
+}
+
+// Byte offset of 16-byte chunk c (0..15) of row r in one half (K or V) of a ring slot.
+__device__ __forceinline__ uint32_t ring_offset(int r, int c) {
+  return static_cast<uint32_t>(r * 256 + ((c ^ (r & 7)) << 4));
 }
 
 __device__ __forceinline__ void attn_sync() {
@@ -151,8 +160,8 @@ __device__ __forceinline__ void norm_rope4(float (&x)[4], const bf16* w, const f
 // One item. tid in [0, 128). pos: this step's position (length = pos + 1); sp from attn_split with
 // sp.splits <= attn_merge_splits(G, s.slots); split < sp.splits; s.slots >= kAttnSlotsMin (slot
 // (i - 1) % slots is refilled with sub-chunk i - 1 + slots after the scores of sub-chunk i, so
-// sub-chunk i was issued before anyone waits for it only with two slots or more). Every thread of the item must call
-// it, with the same seq. The K / V cache rows must be 16-byte aligned (bulk copies).
+// sub-chunk i was issued before anyone waits for it only with two slots or more). Every thread of
+// the item must call it, with the same seq. The K / V caches must be 16-byte aligned.
 template <int G>
 __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, int pos, AttnSplit sp,
                                const AttnSmem<G>& s, AttnSeq& seq, int tid) {
@@ -173,28 +182,30 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
     return;
   }
 
-  // The K / V ring: sub-chunk i of the split (keys begin + 32 i ..) goes to slot (fills + i) % slots.
-  // Only keys already in the cache are copied (the appended key is read from shared memory); rows
-  // of a slot past them hold stale values that the scores mask and P.V skips.
+  // The K / V ring: sub-chunk i of the split (keys begin + 32 i ..) goes to slot (fills + i) % slots,
+  // each thread copying 8 of its 1024 16-byte chunks and arriving on the slot's barrier once they
+  // have landed. Keys not yet in the cache (past the split, or the appended key) are zero-filled
+  // without a read; the appending warp writes the appended key's and value's row before its scores.
   const int nsub = (end - begin + kAttnChunk - 1) / kAttnChunk;
   const int cached_end = appends ? pos : end;
   const uint32_t ring = smem_addr(s.ring);
-  auto issue = [&](int i) {  // thread 0
+  auto issue = [&](int i) {  // every thread
     const uint32_t n = seq.fills + static_cast<uint32_t>(i);
-    const int slot = static_cast<int>(n % static_cast<uint32_t>(s.slots));
+    const uint32_t slot = n % static_cast<uint32_t>(s.slots);
     const int c0 = begin + i * kAttnChunk;
-    const int rows = max(0, min(c0 + kAttnChunk, cached_end) - c0);
-    const uint32_t bytes = static_cast<uint32_t>(rows) * 256u;
-    mbar_expect_tx(&s.bars[slot], 2u * bytes);
-    if (rows > 0) {
-      const uint32_t dst = ring + static_cast<uint32_t>(slot) * kAttnSlotBytes;
-      bulk_copy(dst, k_head + static_cast<int64_t>(c0) * 128, bytes, &s.bars[slot]);
-      bulk_copy(dst + kAttnSlotBytes / 2, v_head + static_cast<int64_t>(c0) * 128, bytes, &s.bars[slot]);
+    const uint32_t kdst = ring + slot * kAttnSlotBytes;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = tid + kAttnThreads * u;  // row idx / 16, chunk idx % 16
+      const int r = idx >> 4, c = idx & 15;
+      const bool in = c0 + r < cached_end;
+      const int64_t src = (in ? static_cast<int64_t>(c0 + r) : 0) * 128 + c * 8;
+      cp_async16(kdst + ring_offset(r, c), k_head + src, in ? 16u : 0u);
+      cp_async16(kdst + kAttnSlotBytes / 2 + ring_offset(r, c), v_head + src, in ? 16u : 0u);
     }
+    cp_async_mbar_arrive(&s.bars[slot]);
   };
-  // (a caller whose threads wrote this scratch before has them fence the async proxy first)
-  if (tid == 0)
-    for (int i = 0; i < min(s.slots, nsub); ++i) issue(i);
+  for (int i = 0; i < min(s.slots, nsub); ++i) issue(i);
 
   // Everything else this item reads first, issued together: q (and, appending, k / v) rows and
   // this position's cos / sin.
@@ -221,19 +232,14 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
 #pragma unroll
     for (int e = 0; e < 4; ++e) s.qs[gi * 128 + lane * 4 + e] = x[e];
   }
+  uint2 knew_raw = make_uint2(0, 0);  // the appended key's 4 dims of this lane (bf16)
   if (append_warp) {
-    float x[4], v[4];
+    float x[4];
     unpack4(kraw, x);
-    unpack4(vraw, v);
     norm_rope4(x, a.k_norm, cs, sn, lane, a.eps);
-    *reinterpret_cast<uint2*>(a.k_cache + (head_base + pos) * 128 + lane * 4) =
-        make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+    knew_raw = make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+    *reinterpret_cast<uint2*>(a.k_cache + (head_base + pos) * 128 + lane * 4) = knew_raw;
     *reinterpret_cast<uint2*>(a.v_cache + (head_base + pos) * 128 + lane * 4) = vraw;
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      s.knew[lane * 4 + e] = x[e];  // already bf16 values
-      s.vnew[lane * 4 + e] = v[e];
-    }
   }
   if (tid < G) {
     s.stat[2 * tid] = -INFINITY;
@@ -242,134 +248,144 @@ __device__ void attention_item(const FusedArgs& a, int split, int kvh, int b, in
   attn_sync();
   if (a.trace && tid == 0) a.trace[0] = globaltimer_ns();
 
-  const int kg = tid >> 4, dc = tid & 15;
-  float o[G][8];
+  // MMA lane roles: g = lane / 4 (a row of the A fragment, a column of B), t = lane % 4.
+  const int g = lane >> 2, t = lane & 3;
+  // q^T as the B operand of the scores (k = dims, n = heads): head g's dims 16 s + 2t (+1, +8, +9).
+  uint32_t qf[8][2];
 #pragma unroll
-  for (int g = 0; g < G; ++g)
+  for (int ks = 0; ks < 8; ++ks) {
+    const float* q = s.qs + g * 128 + ks * 16 + 2 * t;
+    qf[ks][0] = g < G ? pack_bf16x2(q[0], q[1]) : 0u;  // bf16 values already: packing is exact
+    qf[ks][1] = g < G ? pack_bf16x2(q[8], q[9]) : 0u;
+  }
+  // O^T accumulators: dims 32 warp + 16 mt + g (+8), heads 2t, 2t + 1.
+  float o[2][4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[g][i] = 0.f;
+  for (int mt = 0; mt < 2; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
 
   for (int i = 0; i < nsub; ++i) {
     const int c0 = begin + i * kAttnChunk;
     const uint32_t n = seq.fills + static_cast<uint32_t>(i);
     const uint32_t slot = n % static_cast<uint32_t>(s.slots);
     mbar_wait(&s.bars[slot], (n / static_cast<uint32_t>(s.slots)) & 1u, a.err, wait_ns);
-    const unsigned char* ks = s.ring + slot * kAttnSlotBytes;
-    const unsigned char* vs = ks + kAttnSlotBytes / 2;
+    const uint32_t kb = ring + slot * kAttnSlotBytes;
+    const uint32_t vb = kb + kAttnSlotBytes / 2;
     float* sc = s.sc + (i & 1) * G * kAttnChunk;
-    // Scores: 4 lanes per key, 32 dims per lane, read as four 16-byte pieces in a rotated order
-    // that gives the 8 lanes of each quarter-warp 8 different bank groups (key rows are 256 bytes).
-    {
-      const int kk = warp * 8 + (lane >> 2);
-      const int part = lane & 3;
-      const int key = c0 + kk;
-      float dot[G];
-#pragma unroll
-      for (int g = 0; g < G; ++g) dot[g] = 0.f;
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        const int vv = (v + (part >> 1) + 2 * (kk & 1)) & 3;
-        float f[8];
-        if (key == pos) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = s.knew[part * 32 + vv * 8 + e];
-        } else {
-          unpack8(*reinterpret_cast<const uint4*>(ks + kk * 256 + part * 64 + vv * 16), f);
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-          for (int e = 0; e < 8; ++e) dot[g] += f[e] * s.qs[g * 128 + part * 32 + vv * 8 + e];
+    if (appends && i == nsub - 1) {  // the appended key and value into their (zero-filled) rows
+      if (append_warp) {
+        const int r = pos - c0;
+        const uint32_t off = ring_offset(r, lane >> 1) + (lane & 1) * 8;
+        asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(kb + off), "r"(knew_raw.x), "r"(knew_raw.y) : "memory");
+        asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(vb + off), "r"(vraw.x), "r"(vraw.y) : "memory");
       }
+      attn_sync();
+    }
+    // Scores: warp w < 2 takes keys 16 w .. 16 w + 15 (the MMA's M) over the 128 dims (8 k-steps).
+    if (warp < 2) {
+      float d[4] = {0.f, 0.f, 0.f, 0.f};
+      const int lr = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], 1);
-        dot[g] += __shfl_xor_sync(0xffffffffu, dot[g], 2);
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t a0, a1, a2, a3;
+        ldmatrix_x4(a0, a1, a2, a3, kb + ring_offset(lr, 2 * ks + (lane >> 4)));
+        mma16816(d, a0, a1, a2, a3, qf[ks][0], qf[ks][1]);
       }
-      if (part == 0) {
+      // d: keys 16 w + g (+8), heads 2t, 2t + 1
 #pragma unroll
-        for (int g = 0; g < G; ++g) sc[g * kAttnChunk + kk] = key < end ? dot[g] * kAttnScale : -INFINITY;
+      for (int e = 0; e < 4; ++e) {
+        const int kk = 16 * warp + g + 8 * (e >> 1), head = 2 * t + (e & 1);
+        if (head < G) sc[head * kAttnChunk + kk] = c0 + kk < end ? d[e] * kAttnScale : -INFINITY;
       }
     }
     attn_sync();
     // every thread is past its P.V reads of sub-chunk i - 1: its slot takes sub-chunk i - 1 + slots
-    if (tid == 0 && i >= 1 && i - 1 + s.slots < nsub) issue(i - 1 + s.slots);
+    if (i >= 1 && i - 1 + s.slots < nsub) issue(i - 1 + s.slots);
     // Online softmax per head: running max / sum, this sub-chunk's probabilities and rescale.
-    for (int g = warp; g < G; g += kAttnThreads / 32) {
-      const float sv = sc[g * kAttnChunk + lane];
-      const float m_old = s.stat[2 * g];
+    for (int h = warp; h < G; h += kAttnThreads / 32) {
+      const float sv = sc[h * kAttnChunk + lane];
+      const float m_old = s.stat[2 * h];
       const float m = fmaxf(m_old, warp_max(sv));
       const float p = sv == -INFINITY ? 0.f : expf(sv - m);
       const float l = warp_sum(p);
-      sc[g * kAttnChunk + lane] = p;
+      sc[h * kAttnChunk + lane] = p;
       if (lane == 0) {
         const float al = m_old == -INFINITY ? 0.f : expf(m_old - m);
-        s.alpha[g] = al;
-        s.stat[2 * g] = m;
-        s.stat[2 * g + 1] = s.stat[2 * g + 1] * al + l;
+        s.alpha[h] = al;
+        s.stat[2 * h] = m;
+        s.stat[2 * h + 1] = s.stat[2 * h + 1] * al + l;
       }
     }
     attn_sync();
-    // P.V: thread (key group kg, dims 8 dc ..), keys kg + 8j; keys past the split are skipped.
+    // P.V as O^T += V^T P^T: warp w takes dims 32 w .. 32 w + 31 (two M tiles), the 32 keys as two
+    // k-steps; P^T (k = keys, n = heads) as a high and a low bf16 part.
+    {
+      const float al0 = 2 * t < G ? s.alpha[2 * t] : 0.f;
+      const float al1 = 2 * t + 1 < G ? s.alpha[2 * t + 1] : 0.f;
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const float al = s.alpha[g];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) o[g][e] *= al;
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int kk = kg + 8 * j;
-      const int key = c0 + kk;
-      if (key >= end) continue;
-      float f[8];
-      if (key == pos) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = s.vnew[dc * 8 + e];
-      } else {
-        unpack8(*reinterpret_cast<const uint4*>(vs + kk * 256 + dc * 16), f);
+      for (int mt = 0; mt < 2; ++mt) {
+        o[mt][0] *= al0;
+        o[mt][1] *= al1;
+        o[mt][2] *= al0;
+        o[mt][3] *= al1;
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float p = sc[g * kAttnChunk + kk];
+      for (int kt = 0; kt < 2; ++kt) {
+        float pv[4];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[g][e] += p * f[e];
+        for (int e = 0; e < 4; ++e) pv[e] = g < G ? sc[g * kAttnChunk + 16 * kt + 2 * t + (e & 1) + 8 * (e >> 1)] : 0.f;
+        float hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          hi[e] = bf16_round(pv[e]);
+          lo[e] = pv[e] - hi[e];
+        }
+        const uint32_t bh0 = pack_bf16x2(hi[0], hi[1]), bh1 = pack_bf16x2(hi[2], hi[3]);
+        const uint32_t bl0 = pack_bf16x2(lo[0], lo[1]), bl1 = pack_bf16x2(lo[2], lo[3]);
+        // V^T fragments: matrix j of ldmatrix = value rows 16 kt + 8 (j / 2) .., dims 16 m + 8 (j % 2) ..
+        const int vr = 16 * kt + (lane & 7) + 8 * (lane >> 4);
+#pragma unroll
+        for (int mt = 0; mt < 2; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          ldmatrix_x4_trans(a0, a1, a2, a3, vb + ring_offset(vr, 2 * (2 * warp + mt) + ((lane >> 3) & 1)));
+          mma16816(o[mt], a0, a1, a2, a3, bh0, bh1);
+          mma16816(o[mt], a0, a1, a2, a3, bl0, bl1);
+        }
       }
     }
   }
   seq.fills += static_cast<uint32_t>(nsub);
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s.red[(kg * G + g) * 128 + dc * 8 + i] = o[g][i];
-  attn_sync();
   if (a.trace && tid == 0) a.trace[1] = globaltimer_ns();
 
+  // o[mt][e]: dim 32 warp + 16 mt + g + 8 (e >> 1), head 2t + (e & 1) (heads past G hold zeros).
   if (sp.splits == 1) {
-    for (int i = tid; i < G * 128; i += kAttnThreads) {
-      const int g = i / 128, d = i % 128;
-      float sum = 0.f;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) sum += s.red[(k * G + g) * 128 + d];
-      a.out[(static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * 128 + d] =
-          __float2bfloat16_rn(sum / s.stat[2 * g + 1]);
-    }
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = 32 * warp + 16 * mt + g + 8 * (e >> 1), head = 2 * t + (e & 1);
+        if (head < G)
+          a.out[(static_cast<int64_t>(b) * a.q_heads + kvh * G + head) * 128 + d] =
+              __float2bfloat16_rn(o[mt][e] / s.stat[2 * head + 1]);
+      }
     attn_sync();  // the item's shared scratch may be reused right after
     return;
   }
-  for (int i = tid; i < G * 128; i += kAttnThreads) {
-    const int g = i / 128, d = i % 128;
-    float sum = 0.f;
+  {
+    float* rec0 = a.records + ((static_cast<int64_t>(b) * a.q_heads + kvh * G) * kAttnSplitsMax + split) * kAttnRecord;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) sum += s.red[(k * G + g) * 128 + d];
-    float* rec =
-        a.records + ((static_cast<int64_t>(b) * a.q_heads + kvh * G + g) * kAttnSplitsMax + split) * kAttnRecord;
-    __stcg(rec + d, sum);
-    if (d == 0) {
-      __stcg(rec + 128, s.stat[2 * g]);
-      __stcg(rec + 129, s.stat[2 * g + 1]);
+    for (int mt = 0; mt < 2; ++mt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int d = 32 * warp + 16 * mt + g + 8 * (e >> 1), head = 2 * t + (e & 1);
+        if (head < G) __stcg(rec0 + static_cast<int64_t>(head) * kAttnSplitsMax * kAttnRecord + d, o[mt][e]);
+      }
+    if (tid < G) {
+      __stcg(rec0 + static_cast<int64_t>(tid) * kAttnSplitsMax * kAttnRecord + 128, s.stat[2 * tid]);
+      __stcg(rec0 + static_cast<int64_t>(tid) * kAttnSplitsMax * kAttnRecord + 129, s.stat[2 * tid + 1]);
     }
   }
+  // the merge's bulk copies (async proxy) may overwrite the ring this thread's copies filled
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   // Arrival: the last split of this (row, KV head) merges every split. The records written by
   // every thread are ordered before thread 0's acq_rel fence by the barrier (release); the last
   // arriver's fence after its counter update orders its reads after it (acquire), and the proxy
