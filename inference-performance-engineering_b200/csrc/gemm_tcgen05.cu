@@ -9,6 +9,8 @@
 //               reference rounding, fused residual / SiLU*up / fp32-logit writes
 // Two accumulator buffers in TMEM let the epilogue of tile i overlap the MMAs of tile i+1.
 // Every mbarrier wait is bounded; a timeout sets the device error word and the CTA winds down.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "launch.h"
 #include "tensor_map.h"
@@ -21,7 +23,7 @@ constexpr int kThreads = 192;
 
 template <int BN>
 struct Cfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kStages = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -321,20 +323,66 @@ cudaError_t run_epi(int epi, const CUtensorMap& ma, const CUtensorMap& mb, void*
   }
 }
 
+// 64-column tiles: every epilogue but SiLU*up (its gate / up pairs span 128 columns).
+cudaError_t run_epi64(int epi, const CUtensorMap& ma, const CUtensorMap& mb, void* c, const void* residual, int m,
+                      int n, int k, int* err, cudaStream_t stream) {
+  switch (epi) {
+    case IPE_EPI_STORE: return run<64, IPE_EPI_STORE>(ma, mb, c, residual, m, n, k, err, stream);
+    case IPE_EPI_RESIDUAL: return run<64, IPE_EPI_RESIDUAL>(ma, mb, c, residual, m, n, k, err, stream);
+    case IPE_EPI_PARTIAL: return run<64, IPE_EPI_PARTIAL>(ma, mb, c, residual, m, n, k, err, stream);
+    case IPE_EPI_LOGITS: return run<64, IPE_EPI_LOGITS>(ma, mb, c, residual, m, n, k, err, stream);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 }  // namespace
+
+// Output-tile width: the one with the least wave-quantised time, ceil(tiles / SMs) x BN, weighted
+// by the tile's relative cost per column (a wider tile re-reads A less: 0.8 for 256, 1.15 for 64;
+// fitted to B200 timings of Qwen3-1.7B's layer GEMMs at M = 512 and 4096). At M = 512, o_proj and
+// down_proj (N = 2048) take 64-column tiles: 128 tiles instead of 64 on 148 SMs (-11% and -6%). The
+// SiLU*up epilogue pairs gate / up columns inside 128-column groups, so it takes 128 or 256.
+// IPE_GEMM_BN forces a width where it is valid.
+int pick_bn(int m, int n, int epilogue) {
+  static const int forced = [] {
+    const char* v = std::getenv("IPE_GEMM_BN");
+    return v ? std::atoi(v) : 0;
+  }();
+  const int widths[3] = {256, 128, 64};
+  const float weight[3] = {0.8f, 1.0f, 1.15f};
+  auto valid = [&](int bn) { return n % bn == 0 && (epilogue != IPE_EPI_SILU_MUL || bn >= 128); };
+  if ((forced == 64 || forced == 128 || forced == 256) && valid(forced)) return forced;
+  const int64_t m_tiles = (m + kBM - 1) / kBM;
+  int best = 0;
+  float best_cost = 0.f;
+  for (int i = 0; i < 3; ++i) {
+    if (!valid(widths[i])) continue;
+    const int64_t tiles = m_tiles * (n / widths[i]);
+    const int64_t waves = (tiles + sm_count() - 1) / sm_count();
+    const float cost = static_cast<float>(waves) * widths[i] * weight[i];
+    if (best == 0 || cost < best_cost) {
+      best = widths[i];
+      best_cost = cost;
+    }
+  }
+  return best;
+}
 
 cudaError_t launch_gemm(const void* a, const void* b, void* c, int m, int n, int k, int epilogue, const void* residual,
                         int* err, cudaStream_t stream, const char** message) {
-  // BN 256 halves the A re-reads when there are enough tiles to fill the GPU; BN 128 otherwise.
-  const bool wide = (n % 256 == 0) && (static_cast<int64_t>((m + kBM - 1) / kBM) * (n / 256) >= sm_count());
-  const int bn = wide ? 256 : 128;
+  const int bn = pick_bn(m, n, epilogue);
+  if (bn == 0) {
+    *message = "no output-tile width divides n";
+    return cudaErrorInvalidValue;
+  }
   CUtensorMap ma, mb;
   if (!make_map(&ma, a, m, k, kBM) || !make_map(&mb, b, n, k, bn)) {
     *message = "cuTensorMapEncodeTiled failed (driver entry point missing or bad operand layout)";
     return cudaErrorInvalidValue;
   }
-  return wide ? run_epi<256>(epilogue, ma, mb, c, residual, m, n, k, err, stream)
-              : run_epi<128>(epilogue, ma, mb, c, residual, m, n, k, err, stream);
+  if (bn == 256) return run_epi<256>(epilogue, ma, mb, c, residual, m, n, k, err, stream);
+  if (bn == 128) return run_epi<128>(epilogue, ma, mb, c, residual, m, n, k, err, stream);
+  return run_epi64(epilogue, ma, mb, c, residual, m, n, k, err, stream);
 }
 
 }  // namespace ipe
