@@ -367,7 +367,16 @@ def run_tp(args, rank: int, world: int) -> dict | None:
     with ClockSampler(device.index) as clocks:
         full = [timed(new) for _ in range(args.steps)]
         first = [timed(1) for _ in range(args.steps)]
-    t = torch.tensor([sum(full), sum(first)], dtype=torch.float64, device=device)
+    exchange_us = 0.0
+    if args.tp_allreduce == "fused":  # one traced step: the staging that waits on the peers' parts
+        from ipe_b200 import _native as nat
+        from ipe_b200.steptrace import exchange_stage_us, traced_step
+
+        dist.barrier()
+        raw = traced_step(engine._step_desc(True), nat.load().ipe_decode_step_grid(), QWEN3_1_7B.num_hidden_layers,
+                          stream.cuda_stream, device)
+        exchange_us = exchange_stage_us(raw, QWEN3_1_7B.num_hidden_layers)
+    t = torch.tensor([sum(full), sum(first), exchange_us], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     engine.close()
     if rank != 0:
@@ -381,6 +390,7 @@ def run_tp(args, rank: int, world: int) -> dict | None:
             "config": {"workload": f"W1 tensor parallel: batch {batch}, prompt {prompt}, {new} new tokens",
                        "parallelism": f"tp{world}", "allreduce": args.tp_allreduce},
             "decode_ms_per_token": round(decode_s / ((new - 1) * args.steps) * 1e3, 4),
+            "exchange_stage_us_per_step": round(t[2].item(), 1) if args.tp_allreduce == "fused" else None,
             "clocks": clocks.summary()}
 
 

@@ -200,6 +200,14 @@ __device__ __noinline__ void tp_stage(const StepArgs& a, const TpStage& st, int 
   bool ok = true;
   if (st.norm_w && lane == 0)
     for (int b = 0; b < B; ++b) st.red_ss[cw * 16 + b] = 0.f;
+  // the norm weights of this thread's first 16-column chunk, fetched with the rows and parts (with
+  // hidden = 16 * 128 every chunk of the thread has these columns)
+  const int k_first = tid % chunks;
+  uint4 w_first[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+  if (st.norm_w) {
+    w_first[0] = ldg16(st.norm_w + k_first * 16);
+    w_first[1] = ldg16(st.norm_w + k_first * 16 + 8);
+  }
   for (int i = tid; i < total; i += kCThreads) {  // warp-uniform rows: chunks is a multiple of 32
     const int b = i / chunks, k = i % chunks;
     const bf16* xo = st.x_old + static_cast<int64_t>(b) * H + k * 16;
@@ -247,17 +255,21 @@ __device__ __noinline__ void tp_stage(const StepArgs& a, const TpStage& st, int 
   if (!ok) *st.abort_smem = 1;
   if (st.norm_w) {
     consumers_sync();
-    const int chunks8 = H / 8;
-    for (int i = tid; i < B * chunks8; i += kCThreads) {
-      const int b = i / chunks8, c = i % chunks8;
+    // the same 16-column chunks as above: the norm weights are mostly in registers already
+    for (int i = tid; i < total; i += kCThreads) {
+      const int b = i / chunks, k = i % chunks;
       const float* ss = st.red_ss;
       const float r = rsqrtf((ss[b] + ss[16 + b] + ss[32 + b] + ss[48 + b]) / static_cast<float>(H) + d.eps);
-      float f[8], w[8];
-      unpack8(*reinterpret_cast<const uint4*>(st.xs + b * (H + kPad) + c * 8), f);
-      unpack8(ldg16(st.norm_w + c * 8), w);
+      bf16* row = st.xs + b * (H + kPad) + k * 16;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = w[e] * bf16_round(f[e] * r);
-      *reinterpret_cast<uint4*>(st.xs + b * (H + kPad) + c * 8) = pack8(f);
+      for (int h = 0; h < 2; ++h) {
+        float f[8], w[8];
+        unpack8(*reinterpret_cast<const uint4*>(row + 8 * h), f);
+        unpack8(k == k_first ? w_first[h] : ldg16(st.norm_w + k * 16 + 8 * h), w);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = w[e] * bf16_round(f[e] * r);
+        *reinterpret_cast<uint4*>(row + 8 * h) = pack8(f);
+      }
     }
   }
   consumers_sync();

@@ -60,6 +60,22 @@ def summarize(raw: torch.Tensor, layers: int) -> dict:
     return {"phases": table, "lm_end_us": lm_end, "sampling_tail_us": t[0, words - 1].item() - lm_end}
 
 
+def exchange_stage_us(raw: torch.Tensor, layers: int) -> float:
+    """Tensor-parallel step: microseconds per step that the CTAs spend, on average, between the end of
+    a row-parallel phase (o_proj, down_proj; its parts pushed to every rank) and the next phase's
+    activations staged (the peers' parts received, summed into the residual stream, normalised):
+    the exposed part of the two exchanges of each layer."""
+    t = (raw - raw[:, 0].min()).double() / 1000.0
+    total = 0.0
+    for p in range(2, 5 * layers + 2):
+        kind = KINDS[(p - 2) % 5]
+        if kind not in ("gu", "qkv") or (kind == "qkv" and p == 2):
+            continue
+        b = 1 + 5 * (p - 1)
+        total += (t[:, b - 3] - t[:, b - 4]).mean().item()
+    return total
+
+
 def format_summary(summary: dict, untraced_us: float, label: str) -> str:
     lines = [f"{label}: untraced step {untraced_us:.1f} us; LM head done at {summary['lm_end_us']:.1f} us; "
              f"sampling tail {summary['sampling_tail_us']:.1f} us",

@@ -4,7 +4,7 @@ and the sampling tail, for the word layout IPE_TRACE_WORDS of include/ipe_b200.h
 import torch
 
 from ipe_b200 import _native as nat
-from ipe_b200.steptrace import format_summary, summarize
+from ipe_b200.steptrace import exchange_stage_us, format_summary, summarize
 
 
 def test_summary_of_a_synthetic_trace():
@@ -33,3 +33,23 @@ def test_summary_of_a_synthetic_trace():
     assert phases["attn"][1] == 0.0
     assert abs(summary["sampling_tail_us"] - 0.5) < 1e-9
     assert "sampling tail 0.5 us" in format_summary(summary, 1234.0, "x")
+
+
+def test_exchange_staging_of_a_synthetic_tensor_parallel_trace():
+    # every phase staged 1 us after its start, except the phases that follow an exchange (gate/up,
+    # and QKV from the second layer on), staged 4 us after theirs; 3 layers: 3 + 2 of them
+    layers, grid = 3, 4
+    words = nat.trace_words(layers)
+    raw = torch.zeros(grid, words, dtype=torch.int64)
+    ends = 5 * layers + 2
+    clock = 1_000_000
+    raw[:, 0] = clock
+    for p in range(1, ends + 1):
+        b = 1 + 5 * (p - 1)
+        kind = None if p in (1, ends) else ("qkv", "attn", "o", "gu", "down")[(p - 2) % 5]
+        after_exchange = kind == "gu" or (kind == "qkv" and p > 2)
+        if p > 1:
+            raw[:, b - 3] = clock + (4000 if after_exchange else 1000)
+        raw[:, b] = raw[:, b + 1] = clock + 5000
+        clock += 5000
+    assert abs(exchange_stage_us(raw, layers) - 5 * 4.0) < 1e-9
