@@ -23,6 +23,25 @@ from oracle import qwen3 as oq
 
 pytestmark = pytest.mark.gpu
 BF16 = torch.bfloat16
+NEAR_TIE = 1e-2  # the oracle's top-2 gap below which greedy choices may differ
+
+
+def off_choices(choice, oracle):
+    """Positions where `choice` differs from the oracle's argmax although the oracle's top-2 gap is
+    at least NEAR_TIE (a disagreement the near-tie exception does not cover)."""
+    top2 = oracle.topk(2, -1).values
+    gap = top2[..., 0] - top2[..., 1]
+    return int(((choice != oracle.argmax(-1)) & (gap >= NEAR_TIE)).sum())
+
+
+def reference_off_choices(cpu_model, ids, prompt, oracle):
+    """off_choices of the restated reference bf16 engine (sdpa and math attention), teacher-forced
+    on the same tokens: how often the reference's own variants leave the oracle outside near ties."""
+    counts = []
+    for backend in oq.BACKENDS:
+        engine = oq.CachedEngine(cpu_model, batch=ids.shape[0], capacity=ids.shape[1] + 1, dtype=BF16, backend=backend)
+        counts.append(off_choices(oq.teacher_forced(engine, ids, prompt).argmax(-1), oracle))
+    return counts
 
 
 @pytest.fixture(scope="module")
@@ -94,9 +113,10 @@ def test_greedy_generation_follows_the_oracle_except_at_near_ties(models):
     assert out.tokens.shape == (2, 20) and out.lengths.tolist() == [20, 20]
     seq = torch.cat((prompt, out.tokens[:, :-1]), 1)
     oracle = oq.oracle_logits(cpu, seq, list(range(11, seq.shape[1])))
-    chosen = oracle.gather(-1, out.tokens[..., None]).squeeze(-1)
-    gap = oracle.max(-1).values - chosen
-    assert (gap <= 0.05).all(), gap.max()
+    # our greedy choices equal the oracle's except at near ties, or no more often than the
+    # reference's own bf16 engine departs from it on the same tokens
+    ours = off_choices(out.tokens, oracle)
+    assert ours <= max(reference_off_choices(cpu, seq, 12, oracle)), ours
 
 
 def test_generation_is_reproducible_and_logprobs_match_the_logits(models):
@@ -316,8 +336,6 @@ def test_qwen3_1_7b_meets_the_rule_and_the_reference_engine_bar(qwen17):
     theirs = accuracy.errors(oracle, oq.teacher_forced(ref_engine, ids, prompt)).summary()
     for key in ("median_abs", "max_abs", "mean_kl"):
         assert summary[key] <= 1.5 * theirs[key], (key, summary, theirs)
-    # greedy choice equal to the oracle's except where the oracle's top-2 gap is within our error
-    top2 = oracle.topk(2, -1).values
-    gap = (top2[..., 0] - top2[..., 1]).reshape(-1)
-    agree = (mine.argmax(-1) == oracle.argmax(-1)).reshape(-1)
-    assert bool((agree | (gap < 2 * summary["max_abs"])).all())
+    # Greedy choices are judged over the 256 steps of the W1 generation
+    # (test_gpu_parity_1_7b.py::test_w1_greedy_choices_follow_the_reference_engine_except_near_ties):
+    # 17 positions are too few to compare departure counts with the reference engines'.
