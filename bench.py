@@ -104,8 +104,8 @@ def decode_bytes_per_step(config, batch: int, context: float) -> float:
 # DRAM bytes of one decode_step_kernel launch measured by ncu (dram__bytes_read.sum +
 # dram__bytes_write.sum) on the Qwen3-1.7B architecture at batch 1, cache position 514, with 1 and
 # 2 decoder layers: the LM-head part and the per-layer part (captures summarised under profiles/).
-NCU_STEP_FIXED_BYTES = 725.64e6 + 4.65e6 - (102.80e6 + 0.45e6)
-NCU_STEP_LAYER_BYTES = 102.80e6 + 0.45e6
+NCU_STEP_LAYER_BYTES = (828.229888e6 + 4.516864e6) - (725.452544e6 + 5.074944e6)
+NCU_STEP_FIXED_BYTES = 725.452544e6 + 5.074944e6 - NCU_STEP_LAYER_BYTES
 NCU_STEP_POSITION = 514
 
 
