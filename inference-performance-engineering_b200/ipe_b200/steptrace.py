@@ -60,6 +60,49 @@ def summarize(raw: torch.Tensor, layers: int) -> dict:
     return {"phases": table, "lm_end_us": lm_end, "sampling_tail_us": t[0, words - 1].item() - lm_end}
 
 
+def detail(raw: torch.Tensor, layers: int) -> dict:
+    """Per phase kind, microseconds summed over the step's layers, means over the CTAs that stamped
+    them (a CTA without units in a phase leaves its tile stamps at zero): [phase span (first CTA's
+    start to the next phase's first release), stage (start to activations staged), to first stage
+    (staged to the first weight stage ready; attention: the first item's q ready to its P.V done),
+    stream (first to last weight stage ready; attention: P.V done to the item merged), tail (last
+    stage to the barrier arrival), barrier (last arrival to first release)]."""
+    t = (raw - raw[:, 0].min()).double() / 1000.0
+    t[raw == 0] = float("nan")
+    ends = 5 * layers + 2
+    table: dict[str, list[float]] = {}
+
+    def mean(x):
+        x = x[~torch.isnan(x)]
+        return x.mean().item() if len(x) else 0.0
+
+    def valid(x):
+        return x[~torch.isnan(x)]
+
+    for p in range(2, ends + 1):
+        b = 1 + 5 * (p - 1)
+        kind = "lm" if p == ends else KINDS[(p - 2) % 5]
+        rel, staged, first, last, arr, nxt = t[:, b - 4], t[:, b - 3], t[:, b - 2], t[:, b - 1], t[:, b], t[:, b + 1]
+        row = table.setdefault(kind, [0.0] * 6)
+        end = valid(nxt if p < ends else arr).max() if p < ends else valid(arr).max()
+        row[0] += (end - valid(rel).min()).item()
+        row[1] += mean(staged - rel)
+        row[2] += mean(first - staged)
+        row[3] += mean(last - first)
+        row[4] += mean(arr - torch.where(torch.isnan(last), staged, last))
+        if p < ends:
+            row[5] += (valid(nxt).min() - valid(arr).max()).item()
+    return table
+
+
+def format_detail(table: dict) -> str:
+    lines = [f"{'phase':6s} {'span':>8s} {'stage':>8s} {'to first':>8s} {'stream':>8s} {'tail':>8s} {'barrier':>8s}"
+             "   (us, summed over the step; means over CTAs)"]
+    for kind, row in table.items():
+        lines.append(f"{kind:6s} " + " ".join(f"{v:8.1f}" for v in row))
+    return "\n".join(lines)
+
+
 def exchange_stage_us(raw: torch.Tensor, layers: int) -> float:
     """Tensor-parallel step: microseconds per step that the CTAs spend, on average, between the end of
     a row-parallel phase (o_proj, down_proj; its parts pushed to every rank) and the next phase's
@@ -95,6 +138,7 @@ def main() -> None:
     parser.add_argument("--batch", type=int, default=1)
     parser.add_argument("--prompt", type=int, default=512)
     parser.add_argument("--tp", action="store_true", help="tensor-parallel fused step over the torchrun ranks")
+    parser.add_argument("--detail", action="store_true", help="also print the per-phase means over the CTAs")
     args = parser.parse_args()
     rank, world = int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
     device = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -137,15 +181,21 @@ def main() -> None:
     summary = summarize(raw, layers)
     if args.tp:
         gathered = [None] * world
-        dist.all_gather_object(gathered, (summary, untraced, error))
+        extra = (exchange_stage_us(raw, layers), detail(raw, layers) if args.detail else None)
+        dist.all_gather_object(gathered, (summary, untraced, error, extra))
         if rank == 0:
-            for r, (s, u, err) in enumerate(gathered):
+            for r, (s, u, err, (exchange, table)) in enumerate(gathered):
                 print(format_summary(s, u, f"rank {r} of {world} (device error {err})"), flush=True)
+                print(f"staging after the exchanges: {exchange:.1f} us per step (mean over CTAs)", flush=True)
+                if table is not None:
+                    print(format_detail(table), flush=True)
         engine.close()
         torch.cuda.synchronize()
         dist.destroy_process_group()
     else:
         print(format_summary(summary, untraced, f"one GPU, batch {args.batch} (device error {error})"), flush=True)
+        if args.detail:
+            print(format_detail(detail(raw, layers)), flush=True)
 
 
 if __name__ == "__main__":

@@ -4,7 +4,7 @@ and the sampling tail, for the word layout IPE_TRACE_WORDS of include/ipe_b200.h
 import torch
 
 from ipe_b200 import _native as nat
-from ipe_b200.steptrace import exchange_stage_us, format_summary, summarize
+from ipe_b200.steptrace import detail, exchange_stage_us, format_detail, format_summary, summarize
 
 
 def test_summary_of_a_synthetic_trace():
@@ -53,3 +53,28 @@ def test_exchange_staging_of_a_synthetic_tensor_parallel_trace():
         raw[:, b] = raw[:, b + 1] = clock + 5000
         clock += 5000
     assert abs(exchange_stage_us(raw, layers) - 5 * 4.0) < 1e-9
+
+
+def test_detail_of_a_synthetic_trace():
+    # every phase: staged 1 us after its start, first stage 0.5 us later, last stage 2 us after that,
+    # arrival 0.25 us after the last stage, release 0.25 us after the arrival
+    layers, grid = 2, 2
+    words = nat.trace_words(layers)
+    raw = torch.zeros(grid, words, dtype=torch.int64)
+    ends = 5 * layers + 2
+    clock = 1_000_000
+    raw[:, 0] = clock
+    for p in range(1, ends + 1):
+        b = 1 + 5 * (p - 1)
+        if p > 1:
+            raw[:, b - 3] = clock + 1000
+            raw[:, b - 2] = clock + 1500
+            raw[:, b - 1] = clock + 3500
+        raw[:, b] = clock + 3750
+        raw[:, b + 1] = clock + 4000
+        clock += 4000
+    table = detail(raw, layers)
+    span, stage, first, stream, tail, barrier = table["gu"]
+    assert abs(span - 2 * 4.0) < 1e-9 and abs(stage - 2 * 1.0) < 1e-9 and abs(first - 2 * 0.5) < 1e-9
+    assert abs(stream - 2 * 2.0) < 1e-9 and abs(tail - 2 * 0.25) < 1e-9 and abs(barrier - 2 * 0.25) < 1e-9
+    assert "stream" in format_detail(table)
