@@ -9,10 +9,10 @@
 // boundary: a unit's weights are one contiguous run of half tiles (stream_tile.cuh), streamed in
 // 32 KB bulk copies into a ring of shared-memory stages that all four consumer warps read. Copies
 // that large are what lets one SM's copy engine keep up with its share of HBM (8 KB copies cap the
-// whole GPU near 4.9 TB/s, 32 KB ones reach 7.3 TB/s). A short window of the stages past the
-// ring's copies is prefetched into L2 (a deep one only lengthened every L2 round trip), so HBM
-// keeps streaming while the ring is full at a phase boundary. The consumer warps wait only where
-// the data requires it:
+// whole GPU near 4.9 TB/s, 32 KB ones reach 7.3 TB/s). Nothing is prefetched into L2 by default
+// (weights past the ring, or each layer's K / V rows): every such prefetch measured slower, as it
+// lengthens the L2 round trips of the phase boundaries. The consumer warps wait only where the
+// data requires it:
 // at a bounded-spin grid barrier after each phase (the next phase needs the full activation
 // vector), then they stage that vector in shared memory and consume stages that are usually
 // already there.
@@ -1129,24 +1129,26 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // Tuning of the weight stream, fixed per process (measured on B200 with Qwen3-1.7B at batch 1, a
 // 512-token context): 32 KB ring stages (IPE_STEP_STAGES, 6, fewer when the activations need the
 // room), the producer's L2 prefetch of each layer's K / V rows and norm weights
-// (IPE_STEP_PREFETCH_KV, 1), weight copies marked L2 evict-first (IPE_STEP_EVICT_FIRST, 1),
+// (IPE_STEP_PREFETCH_KV, 0), weight copies marked L2 evict-first (IPE_STEP_EVICT_FIRST, 1),
 // half-row-block units (IPE_STEP_HALF, 1), bulk-copy staging of the o_proj / down_proj rows with
 // the residual rows beside them (IPE_STEP_BULK, 1), the grid barrier's lighter fences
 // (IPE_STEP_LIGHT_FENCES, 1), the unit epilogue overlapped with the next unit's tiles
 // (IPE_STEP_OVERLAP, 1), the attention items' K / V ring slots at most (IPE_STEP_ATTN_SLOTS, 4;
 // as many as fit beside the weight stages), and the stages the producer keeps prefetched into L2
-// past its copies (IPE_STEP_L2_AHEAD, 4: batch 1 / 4 / 16 -1.2 / -2.0 / -0.6 % against none,
-// measured on one box; 16 stages ahead lengthened the step by 2-5 %).
+// past its copies (IPE_STEP_L2_AHEAD, 0). With the attention items streaming their K / V rows
+// through their own ring, both prefetches off measured fastest (batch 1 / 4 / 16: 1116.4 / 1390.8
+// / 3184.8 us per step against 1136.8 / 1404.3 / 3234.1 with both on, one box, medians of 3 and
+// 2 runs): the per-layer K / V burst delayed the grid barrier that precedes it.
 struct StepTuning {
   int stages = 6;
-  int prefetch_kv = 1;
+  int prefetch_kv = 0;
   int evict_first = 1;
   int halves = 1;
   int bulk = 1;
   int light_fences = 1;
   int overlap_epilogue = 1;
   int attn_slots = 4;
-  int l2_ahead = 4;
+  int l2_ahead = 0;
 };
 
 const StepTuning& tuning() {
