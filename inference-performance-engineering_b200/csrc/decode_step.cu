@@ -64,7 +64,7 @@ struct StepArgs {
   int act_cols;             // without ACT_SMEM: RMS-normalised phases with K <= act_cols still stage in shared memory
   int bulk_stage;           // with ACT_SMEM: phases without a norm stage their rows by bulk copies (batch > 1)
   unsigned xres_off;        // bulk staging: byte offset from the scratch of a copy of the residual rows x (0: none)
-  int light_fences;         // grid barrier: acq_rel fence before the arrival, no fence after the acquire load
+  int light_fences;         // grid barrier arrival: 2 release reduction, 1 acq_rel fence + atomic, 0 full fences
   int overlap_epilogue;     // warps 1-3 start the next unit while warp 0 runs this unit's epilogue
   float* cta_records;       // [grid][batch][IPE_PARTIAL_WORDS]: each CTA's merge of its LM-head records
   uint64_t wait_ns;         // bound of every spin-wait
@@ -90,15 +90,23 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
   consumers_sync();
   if (tid == 0) {
     if (tr) tr[0] = globaltimer_ns();
-    // release: the consumer warps' writes (ordered before by the named barrier) before the arrival
-    if (a.light_fences) asm volatile("fence.acq_rel.gpu;" ::: "memory");
-    else __threadfence();
-    atomicAdd(&a.grid_bar[0], 1u);
+    // release: the consumer warps' writes (ordered before by the named barrier) before the arrival.
+    // light_fences 2: one release reduction (no returned value to wait for) and a poll of the count
+    // alone, the abort flag checked with the clock every 64 polls; 1: an acq_rel fence, then the
+    // atomic; 0: full fences on both sides.
+    const bool red_arrive = a.light_fences == 2;
+    if (red_arrive) {
+      asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(&a.grid_bar[0]), "r"(1u) : "memory");
+    } else {
+      if (a.light_fences) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+      else __threadfence();
+      atomicAdd(&a.grid_bar[0], 1u);
+    }
     const unsigned target = index * gridDim.x;
     uint64_t start = 0;
     for (unsigned i = 0;; ++i) {
       if (ld_acquire(&a.grid_bar[0]) >= target) break;
-      if (ld_acquire(&a.grid_bar[1])) {
+      if ((!red_arrive || (i & 63u) == 63u) && ld_acquire(&a.grid_bar[1])) {
         *abort_smem = 1;
         break;
       }
@@ -112,7 +120,7 @@ __device__ bool grid_sync(const StepArgs& a, unsigned index, int tid, int* abort
           break;
         }
       }
-      __nanosleep(64);
+      if (!red_arrive) __nanosleep(64);
     }
     // the acquire load that saw the count already orders this CTA's later reads (through the
     // named barrier below); the full fence is kept as the measured alternative
@@ -1131,8 +1139,10 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // room), the producer's L2 prefetch of each layer's K / V rows and norm weights
 // (IPE_STEP_PREFETCH_KV, 0), weight copies marked L2 evict-first (IPE_STEP_EVICT_FIRST, 1),
 // half-row-block units (IPE_STEP_HALF, 1), bulk-copy staging of the o_proj / down_proj rows with
-// the residual rows beside them (IPE_STEP_BULK, 1), the grid barrier's lighter fences
-// (IPE_STEP_LIGHT_FENCES, 1), the unit epilogue overlapped with the next unit's tiles
+// the residual rows beside them (IPE_STEP_BULK, 1), the grid barrier's arrival
+// (IPE_STEP_LIGHT_FENCES, 2: a release reduction and a poll of the count alone; batch 1 / 4 / 16
+// 1127.9 / 1397.2 / 3073.5 -> 1100.8 / 1374.2 / 3048.5 us per step against 1, an acq_rel fence and
+// an atomic with a poll that also read the abort flag every time; one box, alternating runs), the unit epilogue overlapped with the next unit's tiles
 // (IPE_STEP_OVERLAP, 1), the attention items' K / V ring slots at most (IPE_STEP_ATTN_SLOTS, 4;
 // as many as fit beside the weight stages), and the stages the producer keeps prefetched into L2
 // past its copies (IPE_STEP_L2_AHEAD, 0). With the attention items streaming their K / V rows
@@ -1145,7 +1155,7 @@ struct StepTuning {
   int evict_first = 1;
   int halves = 1;
   int bulk = 1;
-  int light_fences = 1;
+  int light_fences = 2;
   int overlap_epilogue = 1;
   int attn_slots = 4;
   int l2_ahead = 0;
