@@ -46,11 +46,13 @@ constexpr int kThreads = 32 * (kConsumers + 1);
 constexpr int kCThreads = 32 * kConsumers;
 constexpr int kPad = 32;
 constexpr int kStepBarrier = 1;  // named barrier id of the consumer warps
+constexpr int kReadyWord = 32;   // first per-KV-head readiness counter in the barrier words
+constexpr int kReadyHeadsMax = 32;  // the barrier words hold 64 counters; KV heads beyond use the barrier
 constexpr size_t kSmemMax = 226 * 1024;  // dynamic shared memory; the rest holds static arrays
 
 struct StepArgs {
   ipe_decode_step_desc d;
-  unsigned* grid_bar;  // [0] arrivals, [1] abort flag
+  unsigned* grid_bar;  // [0] arrivals, [1] abort flag, [kReadyWord + h] QKV rows of KV head h written (x 16)
   int* attn_counters;
   float* attn_records;
   int* err;
@@ -63,6 +65,7 @@ struct StepArgs {
   int halves;               // half-row-block units allowed
   int act_cols;             // without ACT_SMEM: RMS-normalised phases with K <= act_cols still stage in shared memory
   int bulk_stage;           // with ACT_SMEM: phases without a norm stage their rows by bulk copies (batch > 1)
+  int qkv_ready;            // per-KV-head readiness counters replace the grid barrier after the QKV phase
   unsigned xres_off;        // bulk staging: byte offset from the scratch of a copy of the residual rows x (0: none)
   int light_fences;         // grid barrier arrival: 2 release reduction, 1 acq_rel fence + atomic, 0 full fences
   int overlap_epilogue;     // warps 1-3 start the next unit while warp 0 runs this unit's epilogue
@@ -826,6 +829,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
   const AttnSplit sp = attn_split(pos, a.max_splits);
   const bool res_smem = ACT_SMEM && !TP && a.bulk_stage && a.xres_off != 0;
   AttnSeq attn_seq;  // the attention ring's fills and merges so far (the same in every consumer thread)
+  const bool qkv_ready = !TP && a.qkv_ready;
 
   if (!mbar_wait(&desc_bar, 0, a.err, a.wait_ns)) {
     atomicExch(&a.grid_bar[1], 1u);  // every CTA leaves at its next barrier
@@ -863,6 +867,33 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       const AttnSmem<G> sm(scratch, attn_bars, a.attn_slots);
       for (int it = static_cast<int>(blockIdx.x); it < items; it += G_) {
         const int split = it % sp.splits, rest = it / sp.splits;
+        if (qkv_ready) {
+          // every QKV row of this item's KV head written: (G + 2) x 128 rows a layer, 16 a tick
+          if (tid == 0) {
+            const unsigned target = static_cast<unsigned>((G + 2) * 8 * (layer + 1));
+            const unsigned* word = &a.grid_bar[kReadyWord + rest % d.kv_heads];
+            uint64_t start = 0;
+            for (unsigned i = 0;; ++i) {
+              if (ld_acquire(word) >= target) break;
+              if ((i & 63u) == 63u) {
+                if (ld_acquire(&a.grid_bar[1])) {
+                  *abort_smem = 1;
+                  break;
+                }
+                const uint64_t now = globaltimer_ns();
+                if (start == 0) start = now;
+                else if (now - start > a.wait_ns) {
+                  report(a.err, kErrWaitTimeout);
+                  atomicExch(&a.grid_bar[1], 1u);
+                  *abort_smem = 1;
+                  break;
+                }
+              }
+            }
+          }
+          consumers_sync();
+          if (*abort_smem != 0) return;
+        }
         // the first item's milestones: K / V requested and q ready, scores and P.V done, merged
         fa.trace = trace && it == static_cast<int>(blockIdx.x) ? trace + 1 + 5 * (barrier_index - 1) + 2 : nullptr;
         attention_item<G>(fa, split, rest % d.kv_heads, rest / d.kv_heads, pos, sp, sm, attn_seq, tid);
@@ -883,6 +914,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
       case 0:
         src = x, norm_w = static_cast<const bf16*>(L.input_layernorm), K = H, epi = kGemvStore;
         ea = EpilogueArgs{qkv, QKV, QKV, B, nullptr, nullptr, 0.f, 0};
+        barrier = !qkv_ready;  // the attention items wait for their own head's rows instead
         break;
       case 2:
         src = attn, norm_w = nullptr, K = Q, epi = kGemvResidual, barrier = !tp;
@@ -1010,7 +1042,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const StepArgs
             }
         const int rb = ph.half ? u >> 1 : u, first_half = ph.half ? (u & 1) : 0, halves = ph.half ? 1 : 2;
         if (epi == kGemvResidual && tp) push_parts(acc, rb, first_half, halves);  // this rank's part
-        else if (epi == kGemvStore) row_block_epilogue<kGemvStore, NT>(acc, rb, lane, ea, first_half, halves);
+        else if (epi == kGemvStore) {
+          row_block_epilogue<kGemvStore, NT>(acc, rb, lane, ea, first_half, halves);
+          if (qkv_ready) {  // this unit's QKV rows are written: count them (16 rows a tick) for their KV head
+            __syncwarp();
+            if (lane == 0) {
+              const int r0 = rb * 32 + first_half * 16, kvr = d.kv_heads * 128;
+              const int h = r0 < Q ? r0 / (Q / d.kv_heads) : (r0 < Q + kvr ? (r0 - Q) / 128 : (r0 - Q - kvr) / 128);
+              asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(&a.grid_bar[kReadyWord + h]),
+                           "r"(static_cast<unsigned>(halves))
+                           : "memory");
+            }
+          }
+        }
         else if (epi == kGemvResidual) row_block_epilogue<kGemvResidual, NT>(acc, rb, lane, ea, first_half, halves);
         else row_block_epilogue<kGemvSiluMul, NT>(acc, rb, lane, ea);
       }
@@ -1143,7 +1187,9 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // (IPE_STEP_LIGHT_FENCES, 2: a release reduction and a poll of the count alone; batch 1 / 4 / 16
 // 1127.9 / 1397.2 / 3073.5 -> 1100.8 / 1374.2 / 3048.5 us per step against 1, an acq_rel fence and
 // an atomic with a poll that also read the abort flag every time; one box, alternating runs), the unit epilogue overlapped with the next unit's tiles
-// (IPE_STEP_OVERLAP, 1), the attention items' K / V ring slots at most (IPE_STEP_ATTN_SLOTS, 4;
+// (IPE_STEP_OVERLAP, 1), per-KV-head readiness counters instead of the grid barrier after the QKV
+// phase (IPE_STEP_QKV_READY, 1: batch 1 / 4 / 16 1129.3 / 1416.6 / 3078.6 -> 1118.8 / 1399.1 /
+// 3064.0 us per step, one box, alternating runs), the attention items' K / V ring slots at most (IPE_STEP_ATTN_SLOTS, 4;
 // as many as fit beside the weight stages), and the stages the producer keeps prefetched into L2
 // past its copies (IPE_STEP_L2_AHEAD, 0). With the attention items streaming their K / V rows
 // through their own ring, both prefetches off measured fastest (batch 1 / 4 / 16: 1116.4 / 1390.8
@@ -1159,6 +1205,7 @@ struct StepTuning {
   int overlap_epilogue = 1;
   int attn_slots = 4;
   int l2_ahead = 0;
+  int qkv_ready = 1;
 };
 
 const StepTuning& tuning() {
@@ -1173,6 +1220,7 @@ const StepTuning& tuning() {
     if (const char* v = std::getenv("IPE_STEP_OVERLAP")) r.overlap_epilogue = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_ATTN_SLOTS")) r.attn_slots = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_L2_AHEAD")) r.l2_ahead = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_QKV_READY")) r.qkv_ready = std::atoi(v);
     return r;
   }();
   return t;
@@ -1270,6 +1318,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
   const size_t scratch = scratch_with(slots);
   a.prefetch_kv = tuning().prefetch_kv;
   a.l2_ahead = std::max(0, std::min(64, tuning().l2_ahead));
+  a.qkv_ready = tuning().qkv_ready && d.tp_world <= 1 && d.kv_heads <= kReadyHeadsMax;
   a.evict_first = tuning().evict_first;
   a.halves = tuning().halves;
   a.light_fences = tuning().light_fences;
@@ -1288,7 +1337,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
     a.recv_rec = a.recv_x + tp_parts_bytes(d.tp_world, d.batch, d.hidden);
   }
   // the grid barrier counts arrivals from zero every step ([0] arrivals, [1] abort)
-  cudaError_t e = cudaMemsetAsync(a.grid_bar, 0, 2 * sizeof(unsigned), stream);
+  cudaError_t e = cudaMemsetAsync(a.grid_bar, 0, (a.qkv_ready ? 64 : 2) * sizeof(unsigned), stream);
   if (e != cudaSuccess) return e;
   if (d.tp_world > 1) return nt == 1 ? by_group<1, true, true>(a, smem, stream) : by_group<2, true, true>(a, smem, stream);
   if (nt == 1) return act_smem ? by_group<1, true, false>(a, smem, stream) : by_group<1, false, false>(a, smem, stream);
