@@ -1189,7 +1189,9 @@ cudaError_t by_group(const StepArgs& a, size_t smem, cudaStream_t stream) {
 // an atomic with a poll that also read the abort flag every time; one box, alternating runs), the unit epilogue overlapped with the next unit's tiles
 // (IPE_STEP_OVERLAP, 1), per-KV-head readiness counters instead of the grid barrier after the QKV
 // phase (IPE_STEP_QKV_READY, 1: batch 1 / 4 / 16 1129.3 / 1416.6 / 3078.6 -> 1118.8 / 1399.1 /
-// 3064.0 us per step, one box, alternating runs), the attention items' K / V ring slots at most (IPE_STEP_ATTN_SLOTS, 4;
+// 3064.0 us per step, one box, alternating runs), a cap on the attention splits per (row, KV head)
+// (IPE_STEP_ATTN_SPLITS, 0 = none: as many as fill the grid measured fastest, batch 1 1119.1 us
+// against 1147.6 with 9 and 1174.2 with 6), the attention items' K / V ring slots at most (IPE_STEP_ATTN_SLOTS, 4;
 // as many as fit beside the weight stages), and the stages the producer keeps prefetched into L2
 // past its copies (IPE_STEP_L2_AHEAD, 0). With the attention items streaming their K / V rows
 // through their own ring, both prefetches off measured fastest (batch 1 / 4 / 16: 1116.4 / 1390.8
@@ -1206,6 +1208,7 @@ struct StepTuning {
   int attn_slots = 4;
   int l2_ahead = 0;
   int qkv_ready = 1;
+  int attn_splits = 0;
 };
 
 const StepTuning& tuning() {
@@ -1221,6 +1224,7 @@ const StepTuning& tuning() {
     if (const char* v = std::getenv("IPE_STEP_ATTN_SLOTS")) r.attn_slots = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_L2_AHEAD")) r.l2_ahead = std::atoi(v);
     if (const char* v = std::getenv("IPE_STEP_QKV_READY")) r.qkv_ready = std::atoi(v);
+    if (const char* v = std::getenv("IPE_STEP_ATTN_SPLITS")) r.attn_splits = std::atoi(v);
     return r;
   }();
   return t;
@@ -1314,6 +1318,7 @@ cudaError_t launch_decode_step(const ipe_decode_step_desc& d, int* err, cudaStre
     ++slots;
   a.attn_slots = slots;
   a.max_splits = std::min(attn_max_splits(sm_count(), d.batch, d.kv_heads), attn_merge_splits(group, slots));
+  if (tuning().attn_splits > 0) a.max_splits = std::min(a.max_splits, tuning().attn_splits);
   a.xres_off = xres ? static_cast<unsigned>(round16(base_scratch(slots))) : 0u;
   const size_t scratch = scratch_with(slots);
   a.prefetch_kv = tuning().prefetch_kv;
