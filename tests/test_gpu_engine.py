@@ -1,8 +1,8 @@
 """The CUDA engine end to end against the oracle and the reference's golden vectors.
 
 Models are the golden-vector models (tests/cases.py) moved to the GPU, and a full 28-layer
-Qwen3-1.7B-architecture random-init model for the north-star bar. The judge of every logit is the
-fp64 oracle on the CPU; the acceptance envelope is the reference's accuracy rule with the oracle's
+Qwen3-1.7B-architecture random-init model for the bar of at most 1.5x the reference bf16 engine's
+errors. Every logit is checked against the fp64 oracle on the CPU; the acceptance envelope is the reference's accuracy rule with the oracle's
 bf16 uncached variants (math, sdpa) as the references (tests/needs_torch/accuracy.py:31-45).
 """
 
@@ -336,6 +336,6 @@ def test_qwen3_1_7b_meets_the_rule_and_the_reference_engine_bar(qwen17):
     theirs = accuracy.errors(oracle, oq.teacher_forced(ref_engine, ids, prompt)).summary()
     for key in ("median_abs", "max_abs", "mean_kl"):
         assert summary[key] <= 1.5 * theirs[key], (key, summary, theirs)
-    # Greedy choices are judged over the 256 steps of the W1 generation
+    # Greedy choices are checked over the 256 steps of the W1 generation
     # (test_gpu_parity_1_7b.py::test_w1_greedy_choices_follow_the_reference_engine_except_near_ties):
     # 17 positions are too few to compare departure counts with the reference engines'.

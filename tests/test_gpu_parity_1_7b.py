@@ -1,6 +1,6 @@
 """Parity of the full 28-layer Qwen3-1.7B-architecture model at the benchmark contexts.
 
-The judge of every logit is the reference's fp64 oracle, `lm_logits(final_hidden(float64))`
+Every logit is checked against the reference's fp64 oracle, `lm_logits(final_hidden(float64))`
 (src/ipe/forward.py:133-152), run on the GPU in fp64 and anchored to the CPU oracle on a short
 prefix (tests/needs_torch/test_gpu.py:72-78). At the W1 context (prompt 512, then teacher-forced
 decode steps) and the W3 context (prompt 4096, the tcgen05 prefill, then decode steps) the engine's

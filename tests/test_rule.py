@@ -2,7 +2,7 @@
 reorderings the way the reference's rule does (tests/needs_torch/test_engine.py:130-188).
 
 Candidates are the oracle's cached engine with one defect planted (on the CPU, in the oracle);
-references are the oracle's uncached bf16/fp32 variants; the judge is the fp64 oracle.
+references are the oracle's uncached bf16/fp32 variants; every error is measured against the fp64 oracle.
 """
 
 import dataclasses
