@@ -2,7 +2,7 @@
 reference's own fp32 results in the golden fixtures and the fp64 oracle.
 
 The envelope is the reference's accuracy rule (tests/needs_torch/accuracy.py:31-45) with the
-reference's fp32 uncached forwards (math, sdpa) as references, and the north-star bar: the cached
+reference's fp32 uncached forwards (math, sdpa) as references, and the 1.5x bar: the cached
 engine's error at most 1.5x the reference fp32 engine's on the same inputs."""
 
 import pytest
